@@ -1,0 +1,683 @@
+// C ABI of libdiffrast_cuda.so (declared in include/diffrast_cuda.h).
+//
+// Host side of the B200 rasterizer: argument checks that mirror the reference's
+// (diffrast-py/src/lib.rs:162-195, 256-273, 344-361; diffrast-gpu/src/lib.rs:914-929),
+// a per-context scratch pool with hit/miss counters (BufferPool, lib.rs:130-188),
+// the launch sequence of each entry point, and the on-device fit loop.
+
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/diffrast_cuda.h"
+#include "dr_device.cuh"
+#include "dr_internal.h"
+
+using namespace dr;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+dr_status fail(dr_status s, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+dr_status cuda_fail(cudaError_t e, const char* what) {
+  if (e == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    return fail(DR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
+  }
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver)
+    return fail(DR_NO_DEVICE, "%s: %s", what, cudaGetErrorString(e));
+  return fail(DR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define DR_CUDA(call, what)                       \
+  do {                                            \
+    cudaError_t e_ = (call);                      \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+// Limits: 16-bit-safe tile math and the CUDA grid's y dimension.
+constexpr int kMaxSide = 32768;
+constexpr int kMaxBatch = 65535;
+constexpr long long kMaxTris = 1 << 24;
+constexpr int kTileSide = 16;
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// One named, grow-only device buffer. A request that fits is a pool hit.
+struct Slot {
+  void* ptr = nullptr;
+  size_t cap = 0;
+};
+
+}  // namespace
+
+struct dr_ctx {
+  int device = 0;
+  std::mutex mu;
+  int bg_on_device = 0;
+  uint64_t hits = 0, misses = 0;
+  Slot recs, partials, counters, bgbuf;
+  // fit state
+  Slot fit_params, fit_m, fit_v, fit_grads, fit_losses, fit_state;
+  cudaStream_t capture_stream = nullptr;
+  cudaGraphExec_t fit_exec = nullptr;
+  std::vector<unsigned char> fit_key;
+
+  ~dr_ctx() {}
+};
+
+namespace {
+
+dr_status ensure(dr_ctx* c, Slot& s, size_t bytes, bool zero) {
+  if (bytes == 0) bytes = 16;
+  if (s.cap >= bytes) {
+    c->hits++;
+    return DR_OK;
+  }
+  c->misses++;
+  if (s.ptr) {
+    cudaDeviceSynchronize();  // the old buffer may still be in use by queued work
+    cudaFree(s.ptr);
+    s.ptr = nullptr;
+    s.cap = 0;
+  }
+  size_t want = bytes + bytes / 4;  // headroom for slowly growing shapes
+  cudaError_t e = cudaMalloc(&s.ptr, want);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    e = cudaMalloc(&s.ptr, bytes);
+    want = bytes;
+  }
+  if (e != cudaSuccess) {
+    s.ptr = nullptr;
+    return cuda_fail(e, "cudaMalloc(scratch)");
+  }
+  s.cap = want;
+  if (zero) {
+    e = cudaMemset(s.ptr, 0, want);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(scratch)");
+  }
+  return DR_OK;
+}
+
+uint64_t pool_bytes(dr_ctx* c) {
+  uint64_t b = 0;
+  for (Slot* s : {&c->recs, &c->partials, &c->counters, &c->bgbuf, &c->fit_params, &c->fit_m,
+                  &c->fit_v, &c->fit_grads, &c->fit_losses, &c->fit_state})
+    b += s->cap;
+  return b;
+}
+
+void free_slot(Slot& s) {
+  if (s.ptr) cudaFree(s.ptr);
+  s.ptr = nullptr;
+  s.cap = 0;
+}
+
+bool finite_positive(float s) { return std::isfinite(s) && s > 0.0f; }
+
+// Shape/argument checks shared by the batched entry points. Mirrors
+// diffrast-py/src/lib.rs:162-195 (sigma, zero sizes) and the GPU crate's
+// TooLarge conditions.
+dr_status check_common(dr_ctx* ctx, const float* params, int B, int T, int H, int W, float sigma,
+                       int layout) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (B < 0 || T < 0) return fail(DR_INVALID_ARGUMENT, "negative batch or triangle count");
+  if (H <= 0 || W <= 0) return fail(DR_INVALID_ARGUMENT, "height and width must be non-zero");
+  if (!finite_positive(sigma)) return fail(DR_INVALID_ARGUMENT, "sigma must be positive and finite");
+  if (layout != DR_LAYOUT_BHWC && layout != DR_LAYOUT_BCHW)
+    return fail(DR_INVALID_ARGUMENT, "unknown layout %d", layout);
+  if (H > kMaxSide || W > kMaxSide)
+    return fail(DR_TOO_LARGE, "canvas %dx%d exceeds the %d-pixel limit per side", W, H, kMaxSide);
+  if (B > kMaxBatch) return fail(DR_TOO_LARGE, "batch %d exceeds %d", B, kMaxBatch);
+  if ((long long)T > kMaxTris) return fail(DR_TOO_LARGE, "%d triangles exceeds %lld", T, kMaxTris);
+  if ((long long)B * T > (1LL << 28))
+    return fail(DR_TOO_LARGE, "%lld triangles in one batch exceeds %lld", (long long)B * T,
+                1LL << 28);
+  if (B > 0 && T > 0 && !params) return fail(DR_INVALID_ARGUMENT, "null params");
+  return DR_OK;
+}
+
+// Builds the shared part of the raster arguments and runs the set-up kernel.
+dr_status prepare(dr_ctx* ctx, const float* params, const float* background, int bg_per_scene,
+                  int B, int T, int H, int W, float sigma, int layout, int tape, RasterArgs& a,
+                  cudaStream_t s) {
+  memset(&a, 0, sizeof(a));
+  a.B = B;
+  a.T = T;
+  a.H = H;
+  a.W = W;
+  a.tiles_x = (W + kTileSide - 1) / kTileSide;
+  a.tile_row0 = 0;
+  a.tile_row_step = 1;
+  a.sigma_eff = std::fmax(sigma, 1e-8f);  // raster.rs:75 sigma.max(1e-8)
+  a.rej = kRejectSigmas * a.sigma_eff;
+  a.acc = kAcceptSigmas * a.sigma_eff;
+  a.layout = layout;
+  a.n_values = (double)H * (double)W * 3.0;
+  a.grad_scale = 2.0f / (float)((long long)H * W * 3);  // grad.rs:112
+  a.bg_per_scene = bg_per_scene ? 1 : 0;
+  if (!background) {
+    a.bg3[0] = a.bg3[1] = a.bg3[2] = 0.0f;
+  } else if (ctx->bg_on_device) {
+    a.bg_dev = background;
+  } else if (!bg_per_scene) {
+    a.bg3[0] = background[0];
+    a.bg3[1] = background[1];
+    a.bg3[2] = background[2];
+  } else {
+    dr_status st = ensure(ctx, ctx->bgbuf, sizeof(float) * 3 * (size_t)std::max(B, 1), false);
+    if (st) return st;
+    DR_CUDA(cudaMemcpyAsync(ctx->bgbuf.ptr, background, sizeof(float) * 3 * (size_t)B,
+                            cudaMemcpyHostToDevice, s),
+            "copy backgrounds");
+    a.bg_dev = (const float*)ctx->bgbuf.ptr;
+  }
+  size_t rec_bytes = tri_rec_bytes() * (size_t)B * (size_t)T;
+  dr_status st = ensure(ctx, ctx->recs, rec_bytes, false);
+  if (st) return st;
+  a.recs = (const TriRec*)ctx->recs.ptr;
+  DR_CUDA(launch_setup(params, B * T, W, H, sigma, tape, (TriRec*)ctx->recs.ptr, s), "set-up kernel");
+  return DR_OK;
+}
+
+dr_status loss_scratch(dr_ctx* ctx, RasterArgs& a, int n_tiles) {
+  dr_status st = ensure(ctx, ctx->partials, sizeof(double) * (size_t)a.B * n_tiles, false);
+  if (st) return st;
+  st = ensure(ctx, ctx->counters, sizeof(unsigned) * (size_t)a.B, true);
+  if (st) return st;
+  a.loss_partials = (double*)ctx->partials.ptr;
+  a.loss_counters = (unsigned*)ctx->counters.ptr;
+  return DR_OK;
+}
+
+dr_status backward_common(dr_ctx* ctx, int mode, const float* params, const float* background,
+                          int bg_per_scene, int B, int T, int H, int W, float sigma,
+                          const float* other, int layout, int shard, int n_shards, float* grads,
+                          float* losses, double* loss_sums, float* image, cudaStream_t s) {
+  dr_status st = check_common(ctx, params, B, T, H, W, sigma, layout);
+  if (st) return st;
+  if (B > 0 && (!other || (T > 0 && !grads)))
+    return fail(DR_INVALID_ARGUMENT, "null target/gradient or grads pointer");
+  if (n_shards < 1 || shard < 0 || shard >= n_shards)
+    return fail(DR_INVALID_ARGUMENT, "shard %d of %d is out of range", shard, n_shards);
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  if (B == 0) return DR_OK;
+  if (T > 0)
+    DR_CUDA(cudaMemsetAsync(grads, 0, sizeof(float) * (size_t)B * T * kParams, s), "zero grads");
+  RasterArgs a;
+  st = prepare(ctx, params, background, bg_per_scene, B, T, H, W, sigma, layout, 1, a, s);
+  if (st) return st;
+  int tiles_y = (H + kTileSide - 1) / kTileSide;
+  a.tile_row0 = shard;
+  a.tile_row_step = n_shards;
+  int rows = tiles_y > shard ? (tiles_y - shard + n_shards - 1) / n_shards : 0;
+  int n_tiles = a.tiles_x * rows;
+  a.other = other;
+  a.grads = grads;
+  a.image = image;
+  a.losses = losses;
+  a.loss_sums = loss_sums;
+  if (mode == kModeLoss) {
+    if (n_tiles == 0) {
+      if (losses) DR_CUDA(cudaMemsetAsync(losses, 0, sizeof(float) * B, s), "zero losses");
+      if (loss_sums) DR_CUDA(cudaMemsetAsync(loss_sums, 0, sizeof(double) * B, s), "zero sums");
+      return DR_OK;
+    }
+    st = loss_scratch(ctx, a, n_tiles);
+    if (st) return st;
+  }
+  DR_CUDA(launch_raster(mode, a, n_tiles, s), "raster kernel");
+  return DR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* dr_last_error(void) { return g_last_error.c_str(); }
+
+const char* dr_status_string(dr_status s) {
+  switch (s) {
+    case DR_OK: return "ok";
+    case DR_INVALID_ARGUMENT: return "invalid argument";
+    case DR_TOO_LARGE: return "too large";
+    case DR_NO_DEVICE: return "no CUDA device";
+    case DR_TIMEOUT: return "timeout";
+    case DR_LAUNCH: return "CUDA launch/runtime error";
+    case DR_COMM: return "collective failed";
+    case DR_OUT_OF_MEMORY: return "out of device memory";
+    case DR_INTERNAL: return "internal error";
+  }
+  return "unknown status";
+}
+
+int dr_params_per_triangle(void) { return kParams; }
+const char* dr_version(void) { return "0.1.0"; }
+
+int dr_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+dr_status dr_device_name(int device, char* buf, size_t len) {
+  if (!buf || len == 0) return fail(DR_INVALID_ARGUMENT, "null buffer");
+  int n = dr_device_count();
+  if (device < 0 || device >= n) return fail(DR_NO_DEVICE, "no CUDA device %d (have %d)", device, n);
+  cudaDeviceProp p;
+  DR_CUDA(cudaGetDeviceProperties(&p, device), "cudaGetDeviceProperties");
+  snprintf(buf, len, "%s", p.name);
+  return DR_OK;
+}
+
+dr_status dr_ctx_create(int device, dr_ctx** out) {
+  if (!out) return fail(DR_INVALID_ARGUMENT, "null output pointer");
+  *out = nullptr;
+  int n = dr_device_count();
+  if (n == 0) return fail(DR_NO_DEVICE, "no CUDA device is visible");
+  if (device < 0 || device >= n) return fail(DR_NO_DEVICE, "no CUDA device %d (have %d)", device, n);
+  DeviceGuard g(device);
+  cudaError_t e = cudaFree(nullptr);  // establish the primary context
+  if (e != cudaSuccess) return cuda_fail(e, "CUDA context initialisation");
+  dr_ctx* c = new dr_ctx();
+  c->device = device;
+  *out = c;
+  return DR_OK;
+}
+
+dr_status dr_ctx_destroy(dr_ctx* c) {
+  if (!c) return DR_OK;
+  {
+    DeviceGuard g(c->device);
+    cudaDeviceSynchronize();
+    for (Slot* s : {&c->recs, &c->partials, &c->counters, &c->bgbuf, &c->fit_params, &c->fit_m,
+                    &c->fit_v, &c->fit_grads, &c->fit_losses, &c->fit_state})
+      free_slot(*s);
+    if (c->fit_exec) cudaGraphExecDestroy(c->fit_exec);
+    if (c->capture_stream) cudaStreamDestroy(c->capture_stream);
+  }
+  delete c;
+  return DR_OK;
+}
+
+dr_status dr_set_background_location(dr_ctx* ctx, int on_device) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  ctx->bg_on_device = on_device ? 1 : 0;
+  return DR_OK;
+}
+
+dr_status dr_render(dr_ctx* ctx, const float* params, const float* background, int bg_per_scene,
+                    int B, int T, int H, int W, float sigma, int layout, float* image,
+                    dr_stream_t stream) {
+  dr_status st = check_common(ctx, params, B, T, H, W, sigma, layout);
+  if (st) return st;
+  if (B > 0 && !image) return fail(DR_INVALID_ARGUMENT, "null image pointer");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  if (B == 0) return DR_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  RasterArgs a;
+  st = prepare(ctx, params, background, bg_per_scene, B, T, H, W, sigma, layout, 0, a, s);
+  if (st) return st;
+  a.image = image;
+  int n_tiles = a.tiles_x * ((H + kTileSide - 1) / kTileSide);
+  DR_CUDA(launch_raster(kModeRender, a, n_tiles, s), "raster kernel");
+  return DR_OK;
+}
+
+dr_status dr_loss_backward(dr_ctx* ctx, const float* params, const float* background,
+                           int bg_per_scene, int B, int T, int H, int W, float sigma,
+                           const float* targets, int layout, float* grads, float* losses,
+                           float* image, dr_stream_t stream) {
+  return backward_common(ctx, kModeLoss, params, background, bg_per_scene, B, T, H, W, sigma,
+                         targets, layout, 0, 1, grads, losses, nullptr, image,
+                         (cudaStream_t)stream);
+}
+
+dr_status dr_grad_backward(dr_ctx* ctx, const float* params, const float* background,
+                           int bg_per_scene, int B, int T, int H, int W, float sigma,
+                           const float* grad_images, int layout, float* grads,
+                           dr_stream_t stream) {
+  return backward_common(ctx, kModeGrad, params, background, bg_per_scene, B, T, H, W, sigma,
+                         grad_images, layout, 0, 1, grads, nullptr, nullptr, nullptr,
+                         (cudaStream_t)stream);
+}
+
+dr_status dr_loss_backward_sharded(dr_ctx* ctx, const float* params, const float* background,
+                                   int bg_per_scene, int B, int T, int H, int W, float sigma,
+                                   const float* targets, int layout, int shard, int n_shards,
+                                   float* grads, double* loss_sums, dr_stream_t stream) {
+  return backward_common(ctx, kModeLoss, params, background, bg_per_scene, B, T, H, W, sigma,
+                         targets, layout, shard, n_shards, grads, nullptr, loss_sums, nullptr,
+                         (cudaStream_t)stream);
+}
+
+dr_status dr_mse_loss(dr_ctx* ctx, const float* images, const float* targets, int B,
+                      int64_t n_per_image, float* losses, dr_stream_t stream) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (B < 0 || n_per_image < 0) return fail(DR_INVALID_ARGUMENT, "negative size");
+  if (B > 0 && (!images || !targets || !losses)) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  if (B > 2147483647) return fail(DR_TOO_LARGE, "batch too large");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  if (B == 0) return DR_OK;
+  DR_CUDA(launch_mse(images, targets, B, (long long)n_per_image, losses, (cudaStream_t)stream),
+          "mse kernel");
+  return DR_OK;
+}
+
+dr_status dr_adam_step(dr_ctx* ctx, float* params, float* m, float* v, const float* grads,
+                       int64_t n, float lr_pos, float lr_color, float lr_alpha, uint32_t step,
+                       float beta1, float beta2, float eps, int project, dr_stream_t stream) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (n < 0) return fail(DR_INVALID_ARGUMENT, "negative length");
+  if (n > 0 && (!params || !m || !v || !grads)) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  if (step == 0) return fail(DR_INVALID_ARGUMENT, "Adam step count starts at 1");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  AdamArgs a;
+  memset(&a, 0, sizeof(a));
+  a.params = params;
+  a.m = m;
+  a.v = v;
+  a.grads = grads;
+  a.n = n;
+  a.lr_pos = lr_pos;
+  a.lr_color = lr_color;
+  a.lr_alpha = lr_alpha;
+  a.beta1 = beta1;
+  a.beta2 = beta2;
+  a.one_minus_beta1 = 1.0f - beta1;
+  a.one_minus_beta2 = 1.0f - beta2;
+  a.eps = eps;
+  // optim.rs:309-310: 1 - beta.powi(t), f32 square-and-multiply.
+  auto powi = [](float base, int e) {
+    float r = 1.0f;
+    for (;;) {
+      if (e & 1) r *= base;
+      e /= 2;
+      if (e == 0) break;
+      base *= base;
+    }
+    return r;
+  };
+  a.bc1 = 1.0f - powi(beta1, (int)step);
+  a.bc2 = 1.0f - powi(beta2, (int)step);
+  a.project = project;
+  DR_CUDA(launch_adam(a, (cudaStream_t)stream), "adam kernel");
+  return DR_OK;
+}
+
+dr_status dr_pool_stats_get(dr_ctx* ctx, dr_pool_stats* out) {
+  if (!ctx || !out) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  out->hits = ctx->hits;
+  out->misses = ctx->misses;
+  out->bytes = pool_bytes(ctx);
+  return DR_OK;
+}
+
+dr_status dr_clear_pool(dr_ctx* ctx) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  cudaDeviceSynchronize();
+  for (Slot* s : {&ctx->recs, &ctx->partials, &ctx->counters, &ctx->bgbuf, &ctx->fit_params,
+                  &ctx->fit_m, &ctx->fit_v, &ctx->fit_grads, &ctx->fit_losses, &ctx->fit_state})
+    free_slot(*s);
+  if (ctx->fit_exec) {
+    cudaGraphExecDestroy(ctx->fit_exec);
+    ctx->fit_exec = nullptr;
+    ctx->fit_key.clear();
+  }
+  return DR_OK;
+}
+
+dr_status dr_stream_wait(dr_stream_t stream, double timeout_s) {
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaStreamQuery((cudaStream_t)stream);
+    if (e == cudaSuccess) return DR_OK;
+    if (e != cudaErrorNotReady) return cuda_fail(e, "stream");
+    double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s)
+      return fail(DR_TIMEOUT, "the GPU did not finish within %.1f s", timeout_s);
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dr_fit: the whole Fitter loop on the device, captured once into a graph.
+// ---------------------------------------------------------------------------
+
+static int validate_fit(const dr_fit_config* c, int T) {  // fit.rs:98-117
+  if (T == 0) return 1;
+  if (!(std::isfinite(c->sigma_start) && std::isfinite(c->sigma_end)) || c->sigma_start <= 0.0f ||
+      c->sigma_end <= 0.0f)
+    return 2;
+  if (c->sigma_start < c->sigma_end) return 3;
+  for (float lr : {c->lr_pos, c->lr_color, c->lr_alpha})
+    if (!std::isfinite(lr) || lr <= 0.0f) return 4;
+  return 0;
+}
+
+static float sigma_at(const dr_fit_config* c, int64_t i) {  // fit.rs:343-349
+  if (c->iters <= 1) return c->sigma_end;
+  float t = (float)i / (float)(c->iters - 1);
+  return c->sigma_start * powf(c->sigma_end / c->sigma_start, t);
+}
+
+dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* init_params,
+                 const float* background, int T, const dr_fit_config* cfg, float* best_params,
+                 float* final_params, float* losses, dr_fit_report* report, dr_stream_t stream) {
+  if (!ctx || !cfg || !report) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  memset(report, 0, sizeof(*report));
+  report->best_loss = INFINITY;
+  int ce = validate_fit(cfg, T);
+  if (ce) {
+    report->config_error = ce;
+    static const char* names[] = {"", "NoTriangles", "NonPositiveSigma", "SigmaNotDecreasing",
+                                  "NonPositiveLearningRate"};
+    return fail(DR_INVALID_ARGUMENT, "invalid fit config: %s", names[ce]);
+  }
+  if (cfg->iters < 0) return fail(DR_INVALID_ARGUMENT, "negative iteration count");
+  dr_status st = check_common(ctx, init_params, 1, T, H, W, cfg->sigma_end, DR_LAYOUT_BHWC);
+  if (st) return st;
+  if (!target || !init_params || !best_params || !final_params || (cfg->iters > 0 && !losses))
+    return fail(DR_INVALID_ARGUMENT, "null pointer");
+  if (cfg->iters > (1 << 24)) return fail(DR_TOO_LARGE, "too many iterations");
+
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t np = (size_t)T * kParams;
+  const int iters = (int)cfg->iters;
+  float bg[3] = {0.f, 0.f, 0.f};
+  if (background) memcpy(bg, background, sizeof(bg));
+
+  if ((st = ensure(ctx, ctx->fit_params, np * 4, false))) return st;
+  if ((st = ensure(ctx, ctx->fit_m, np * 4, false))) return st;
+  if ((st = ensure(ctx, ctx->fit_v, np * 4, false))) return st;
+  if ((st = ensure(ctx, ctx->fit_grads, np * 4, false))) return st;
+  if ((st = ensure(ctx, ctx->fit_losses, (size_t)std::max(iters, 1) * 4, false))) return st;
+  if ((st = ensure(ctx, ctx->fit_state, sizeof(FitState), true))) return st;
+  int tiles = ((W + kTileSide - 1) / kTileSide) * ((H + kTileSide - 1) / kTileSide);
+  if ((st = ensure(ctx, ctx->recs, tri_rec_bytes() * (size_t)T, false))) return st;
+  if ((st = ensure(ctx, ctx->partials, sizeof(double) * (size_t)tiles, false))) return st;
+  if ((st = ensure(ctx, ctx->counters, sizeof(unsigned), true))) return st;
+
+  float* P = (float*)ctx->fit_params.ptr;
+  float* M = (float*)ctx->fit_m.ptr;
+  float* V = (float*)ctx->fit_v.ptr;
+  float* Gr = (float*)ctx->fit_grads.ptr;
+  float* L = (float*)ctx->fit_losses.ptr;
+  FitState* S = (FitState*)ctx->fit_state.ptr;
+
+  // The graph bakes pointers, sizes and the config: reuse it when all match.
+  std::vector<unsigned char> key;
+  auto push = [&](const void* p, size_t n) {
+    const unsigned char* b = (const unsigned char*)p;
+    key.insert(key.end(), b, b + n);
+  };
+  const void* ptrs[] = {target, init_params, best_params, final_params, P, M, V, Gr, L, S,
+                        ctx->recs.ptr, ctx->partials.ptr, ctx->counters.ptr};
+  push(ptrs, sizeof(ptrs));
+  push(cfg, sizeof(*cfg));
+  int dims[3] = {H, W, T};
+  push(dims, sizeof(dims));
+  push(bg, sizeof(bg));
+
+  if (!ctx->fit_exec || key != ctx->fit_key) {
+    if (ctx->fit_exec) {
+      cudaGraphExecDestroy(ctx->fit_exec);
+      ctx->fit_exec = nullptr;
+    }
+    if (!ctx->capture_stream)
+      DR_CUDA(cudaStreamCreateWithFlags(&ctx->capture_stream, cudaStreamNonBlocking),
+              "capture stream");
+    cudaStream_t cs = ctx->capture_stream;
+    DR_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "begin capture");
+    cudaError_t err = cudaSuccess;
+    auto chk = [&](cudaError_t e) {
+      if (err == cudaSuccess && e != cudaSuccess) err = e;
+    };
+    chk(cudaMemcpyAsync(P, init_params, np * 4, cudaMemcpyDeviceToDevice, cs));
+    chk(cudaMemcpyAsync(best_params, init_params, np * 4, cudaMemcpyDeviceToDevice, cs));
+    chk(cudaMemsetAsync(M, 0, np * 4, cs));
+    chk(cudaMemsetAsync(V, 0, np * 4, cs));
+    chk(launch_fit_init(S, cs));
+    for (int i = 0; i < iters; ++i) {
+      float sigma = sigma_at(cfg, i);
+      chk(cudaMemsetAsync(Gr, 0, np * 4, cs));
+      chk(launch_setup(P, T, W, H, sigma, 1, (TriRec*)ctx->recs.ptr, cs));
+      RasterArgs a;
+      memset(&a, 0, sizeof(a));
+      a.recs = (const TriRec*)ctx->recs.ptr;
+      a.B = 1;
+      a.T = T;
+      a.H = H;
+      a.W = W;
+      a.tiles_x = (W + kTileSide - 1) / kTileSide;
+      a.tile_row0 = 0;
+      a.tile_row_step = 1;
+      a.sigma_eff = std::fmax(sigma, 1e-8f);
+      a.rej = kRejectSigmas * a.sigma_eff;
+      a.acc = kAcceptSigmas * a.sigma_eff;
+      a.bg3[0] = bg[0];
+      a.bg3[1] = bg[1];
+      a.bg3[2] = bg[2];
+      a.layout = kLayoutBHWC;
+      a.other = target;
+      a.grad_scale = 2.0f / (float)((long long)H * W * 3);
+      a.grads = Gr;
+      a.loss_partials = (double*)ctx->partials.ptr;
+      a.loss_counters = (unsigned*)ctx->counters.ptr;
+      a.losses = &S->loss;
+      a.n_values = (double)H * (double)W * 3.0;
+      a.skip_flag = &S->stopped;
+      chk(launch_raster(kModeLoss, a, tiles, cs));
+      chk(launch_fit_control(S, i, cfg->min_delta, cfg->patience, L, cs));
+      AdamArgs ad;
+      memset(&ad, 0, sizeof(ad));
+      ad.params = P;
+      ad.m = M;
+      ad.v = V;
+      ad.grads = Gr;
+      ad.n = (long long)np;
+      ad.lr_pos = cfg->lr_pos;
+      ad.lr_color = cfg->lr_color;
+      ad.lr_alpha = cfg->lr_alpha;
+      ad.beta1 = 0.9f;
+      ad.beta2 = 0.999f;
+      ad.one_minus_beta1 = 1.0f - 0.9f;
+      ad.one_minus_beta2 = 1.0f - 0.999f;
+      ad.eps = 1e-8f;
+      // Adam::t equals i + 1 at iteration i: it steps every iteration until
+      // the fit stops, and nothing runs after that.
+      float b1 = 1.0f, b2 = 1.0f, base1 = 0.9f, base2 = 0.999f;
+      for (int e = i + 1;;) {
+        if (e & 1) {
+          b1 *= base1;
+          b2 *= base2;
+        }
+        e /= 2;
+        if (e == 0) break;
+        base1 *= base1;
+        base2 *= base2;
+      }
+      ad.bc1 = 1.0f - b1;
+      ad.bc2 = 1.0f - b2;
+      ad.project = 1;
+      ad.run_flag = &S->run_adam;
+      ad.copy_flag = &S->copy_best;
+      ad.copy_dst = best_params;
+      chk(launch_adam(ad, cs));
+    }
+    chk(cudaMemcpyAsync(final_params, P, np * 4, cudaMemcpyDeviceToDevice, cs));
+    cudaGraph_t graph = nullptr;
+    cudaError_t e_end = cudaStreamEndCapture(cs, &graph);
+    if (err != cudaSuccess || e_end != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      cudaGetLastError();
+      return cuda_fail(err != cudaSuccess ? err : e_end, "capturing the fit loop");
+    }
+    cudaError_t ei = cudaGraphInstantiate(&ctx->fit_exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) {
+      ctx->fit_exec = nullptr;
+      return cuda_fail(ei, "instantiating the fit graph");
+    }
+    ctx->fit_key = key;
+  }
+  DR_CUDA(cudaGraphLaunch(ctx->fit_exec, s), "launching the fit graph");
+  // Bounded wait first (POLL_TIMEOUT semantics), then the blocking reads.
+  st = dr_stream_wait(stream, 600.0);
+  if (st) return st;
+  FitState hs;
+  DR_CUDA(cudaMemcpy(&hs, S, sizeof(hs), cudaMemcpyDeviceToHost), "read fit state");
+  if (hs.count > 0)
+    DR_CUDA(cudaMemcpy(losses, L, sizeof(float) * (size_t)hs.count, cudaMemcpyDeviceToHost),
+            "read losses");
+  report->n_losses = hs.count;
+  report->best_iter = hs.best_iter;
+  report->best_loss = hs.best_loss;
+  report->stop_reason = hs.stopped ? hs.stop_reason : DR_STOP_COMPLETED;
+  return DR_OK;
+}
+
+}  // extern "C"

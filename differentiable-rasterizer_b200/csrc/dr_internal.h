@@ -1,0 +1,80 @@
+// Internal interface between the C ABI (dr_capi.cu) and the kernels
+// (dr_kernels.cu). Not installed; callers use include/diffrast_cuda.h.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace dr {
+
+struct TriRec;
+
+enum RasterMode { kModeRender = 0, kModeLoss = 1, kModeGrad = 2 };
+enum Layout { kLayoutBHWC = 0, kLayoutBCHW = 1 };
+
+struct RasterArgs {
+  const TriRec* recs;  // B*T records from the set-up kernel
+  int B, T, H, W;
+  int tiles_x;
+  int tile_row0, tile_row_step;  // tile rows covered: row0 + i * step
+  float sigma_eff;               // max(sigma, 1e-8) (raster.rs:75)
+  float rej, acc;                // fast-path thresholds (normalized units)
+  float bg3[3];                  // shared background when bg_dev is null
+  const float* bg_dev;           // device background: 3 floats, or B*3 when bg_per_scene
+  int bg_per_scene;
+  int layout;                 // Layout of image / other
+  float* image;               // optional rendered output
+  const float* other;         // target (kModeLoss) or upstream gradient (kModeGrad)
+  float grad_scale;           // 2/N as f32 (grad.rs:112)
+  float* grads;               // (B,T,10), accumulated into (zeroed by the caller)
+  double* loss_partials;      // B * tiles-in-launch scratch
+  unsigned* loss_counters;    // B counters, zero between launches
+  float* losses;              // optional (B,) mean squared error
+  double* loss_sums;          // optional (B,) sum of squared error
+  double n_values;            // H*W*3
+  const int* skip_flag;       // optional: nonzero -> the kernel does nothing
+};
+
+struct AdamArgs {
+  float* params;
+  float* m;
+  float* v;
+  const float* grads;
+  long long n;
+  float lr_pos, lr_color, lr_alpha;
+  float beta1, beta2, one_minus_beta1, one_minus_beta2, eps;
+  float bc1, bc2;  // 1 - beta^t in f32 (optim.rs:309-310)
+  int project;     // fit.rs:399-424 after the update
+  const int* skip_flag;  // optional: nonzero -> no-op
+  const int* run_flag;   // optional: zero -> no update (copy still happens)
+  const int* copy_flag;  // optional: nonzero -> copy_dst <- params first
+  float* copy_dst;
+};
+
+struct FitState {
+  float loss;       // written by the raster kernel each iteration
+  float best_loss;
+  int count;        // losses recorded
+  int since;        // iterations since the last improvement
+  int best_iter;
+  int stopped;
+  int stop_reason;  // 0 Completed, 1 Converged, 2 Diverged
+  int run_adam;
+  int copy_best;
+  int pad[3];
+};
+
+size_t raster_smem_bytes();
+cudaError_t launch_fit_init(FitState* st, cudaStream_t s);
+cudaError_t launch_fit_control(FitState* st, int iter, float min_delta, long long patience,
+                               float* losses, cudaStream_t s);
+size_t tri_rec_bytes();
+cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
+                         int tape_semantics, TriRec* recs, cudaStream_t s);
+cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s);
+cudaError_t launch_mse(const float* img, const float* tgt, int B, long long n, float* losses,
+                       cudaStream_t s);
+cudaError_t launch_adam(const AdamArgs& a, cudaStream_t s);
+
+}  // namespace dr

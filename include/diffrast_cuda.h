@@ -1,0 +1,206 @@
+/*
+ * diffrast_cuda.h - C ABI of libdiffrast_cuda.so, the sm_100a (B200) soft-triangle
+ * rasterizer: batched forward compositing, per-image MSE, analytic backward and a
+ * fused Adam step, for VivianSobers/Differentiable-Rasterizer's hot path.
+ *
+ * This is the drop-in boundary. Every entry point takes plain pointers and sizes;
+ * there are no torch or Rust types in the signatures. Data pointers are DEVICE
+ * memory owned by the caller unless a parameter says "host". Work is enqueued on
+ * `stream` (a cudaStream_t; NULL is the legacy default stream) and returns before
+ * it completes, except where a function says it synchronizes.
+ *
+ * Layouts (identical to the reference's, diffrast-py/src/lib.rs:10-13):
+ *   params  (B, T, 10) f32, per triangle [x0, y0, x1, y1, x2, y2, r, g, b, a],
+ *           vertices in normalized image space (scene.rs:78-92)
+ *   images  (B, H, W, 3) f32 linear RGB (DR_LAYOUT_BHWC, canvas.rs:6-11) or
+ *           (B, 3, H, W) (DR_LAYOUT_BCHW, what torch_layer.rasterize returns)
+ *   background  3 floats shared by the batch, or (B, 3) when bg_per_scene != 0
+ *           (forward_batch.wgsl:18-20); host or device memory both accepted
+ *           (see dr_set_background_location)
+ *
+ * Errors: every function returns a dr_status. A non-OK status leaves a message
+ * for the calling thread in dr_last_error(). Statuses map one to one onto the
+ * reference's GpuError (crates/diffrast-gpu/src/lib.rs:42-72) and its panics.
+ * There is no CPU fallback: a missing or failing device is an error.
+ *
+ * Threading: a context may be used from several threads, but the calls it
+ * serves share its scratch memory, so they must be ordered on ONE stream (or use
+ * one context per stream).
+ */
+#ifndef DIFFRAST_CUDA_H
+#define DIFFRAST_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DR_N_PARAMS 10 /* scene.rs:21 Triangle::N_PARAMS */
+
+#if defined(__GNUC__)
+#define DR_API __attribute__((visibility("default")))
+#else
+#define DR_API
+#endif
+
+typedef struct dr_ctx dr_ctx;
+typedef void* dr_stream_t; /* a cudaStream_t */
+
+/* GpuError (diffrast-gpu/src/lib.rs:42-72) plus the argument panics. */
+typedef enum dr_status {
+  DR_OK = 0,
+  DR_INVALID_ARGUMENT = 1, /* size / shape mismatch, bad sigma (ValueError, asserts) */
+  DR_TOO_LARGE = 2,        /* GpuError::TooLarge (incl. ragged batch, no triangles) */
+  DR_NO_DEVICE = 3,        /* GpuError::NoAdapter */
+  DR_TIMEOUT = 4,          /* GpuError::Timeout (bounded host wait expired) */
+  DR_LAUNCH = 5,           /* a CUDA launch or runtime error (GpuError::DeviceRequest) */
+  DR_COMM = 6,             /* a collective failed (multi-GPU paths) */
+  DR_OUT_OF_MEMORY = 7,    /* device allocation failed */
+  DR_INTERNAL = 8
+} dr_status;
+
+typedef enum dr_layout { DR_LAYOUT_BHWC = 0, DR_LAYOUT_BCHW = 1 } dr_layout;
+
+/* --- context ------------------------------------------------------------ */
+
+/* Creates a context on CUDA device `device`. Replaces GpuRasterizer::new
+ * (diffrast-gpu/src/lib.rs:232-319): there are no pipelines to compile; the
+ * context owns only scratch memory and its reuse pool. */
+DR_API dr_status dr_ctx_create(int device, dr_ctx** out);
+
+/* Waits for the context's device work and frees its scratch. Replaces dropping
+ * the GpuRasterizer / diffrast_rs.shutdown_gpu (diffrast-py/src/lib.rs:435-444). */
+DR_API dr_status dr_ctx_destroy(dr_ctx* ctx);
+
+/* Thread-local message for the last non-OK status on this thread. */
+DR_API const char* dr_last_error(void);
+DR_API const char* dr_status_string(dr_status s);
+
+/* Parameters per triangle (diffrast-py/src/lib.rs:453-456). */
+DR_API int dr_params_per_triangle(void);
+DR_API const char* dr_version(void);
+
+/* Device name into buf (GpuRasterizer::adapter_info, lib.rs:374-376;
+ * diffrast_rs.gpu_adapter, diffrast-py/src/lib.rs:447-450). */
+DR_API dr_status dr_device_name(int device, char* buf, size_t len);
+/* Number of visible CUDA devices (0 when none). */
+DR_API int dr_device_count(void);
+
+/* Where `background` pointers live: 0 = host memory (default), 1 = device. */
+DR_API dr_status dr_set_background_location(dr_ctx* ctx, int on_device);
+
+/* --- hot path ------------------------------------------------------------ */
+
+/* Forward render of a batch into `image` (layout as given).
+ * Replaces GpuRasterizer::render_many (diffrast-gpu/src/lib.rs:615-633) and
+ * diffrast_rs.render_batch (diffrast-py/src/lib.rs:172-231); semantics of
+ * raster::render (crates/diffrast/src/raster.rs:37-68). B == 0 is a no-op. */
+DR_API dr_status dr_render(dr_ctx* ctx, const float* params, const float* background, int bg_per_scene,
+                    int B, int T, int H, int W, float sigma, int layout, float* image,
+                    dr_stream_t stream);
+
+/* Forward + per-image MSE + analytic backward against targets, in one pass.
+ * grads (B,T,10) is overwritten; losses (B,) (may be NULL) receives
+ * mse(render, target) as canvas.rs:45-59 computes it (f64 sum); image (may be
+ * NULL) receives the render. Replaces GpuRasterizer::backward_many
+ * (diffrast-gpu/src/lib.rs:639-816) and diffrast_rs.fused_loss_backward
+ * (diffrast-py/src/lib.rs:331-412); semantics of grad::backward_batch
+ * (crates/diffrast/src/grad.rs:192-207). */
+DR_API dr_status dr_loss_backward(dr_ctx* ctx, const float* params, const float* background,
+                           int bg_per_scene, int B, int T, int H, int W, float sigma,
+                           const float* targets, int layout, float* grads, float* losses,
+                           float* image, dr_stream_t stream);
+
+/* Backward from an upstream image gradient dL/d(image) (same layout rules).
+ * grads (B,T,10) is overwritten. Replaces GpuRasterizer::backward_many_from_grad
+ * (diffrast-gpu/src/lib.rs:828-910) and diffrast_rs.backward_batch
+ * (diffrast-py/src/lib.rs:243-324). */
+DR_API dr_status dr_grad_backward(dr_ctx* ctx, const float* params, const float* background,
+                           int bg_per_scene, int B, int T, int H, int W, float sigma,
+                           const float* grad_images, int layout, float* grads,
+                           dr_stream_t stream);
+
+/* Row-sharded dr_loss_backward for one large scene split across devices: this
+ * call covers the 16-pixel tile rows r with r % n_shards == shard. grads
+ * receives this shard's partial gradient (overwritten); loss_sums (B,) f64
+ * receives this shard's sum of squared error (divide the all-reduced sum by
+ * H*W*3 for the MSE). No reference counterpart: the reference has no
+ * multi-device path; the sum over shards equals dr_loss_backward. */
+DR_API dr_status dr_loss_backward_sharded(dr_ctx* ctx, const float* params, const float* background,
+                                   int bg_per_scene, int B, int T, int H, int W, float sigma,
+                                   const float* targets, int layout, int shard, int n_shards,
+                                   float* grads, double* loss_sums, dr_stream_t stream);
+
+/* Per-image MSE of two (B, n) arrays with an f64 sum.
+ * Replaces GpuRasterizer::encode_loss / loss_batch.wgsl (diffrast-gpu/src/lib.rs:1004-1031)
+ * and Canvas::mse (crates/diffrast/src/canvas.rs:45-59). */
+DR_API dr_status dr_mse_loss(dr_ctx* ctx, const float* images, const float* targets, int B,
+                      int64_t n_per_image, float* losses, dr_stream_t stream);
+
+/* One Adam step (optim.rs:40-60) over n params with the per-parameter rate
+ * pattern of fit.rs:388-396 (index % 10: 0-5 lr_pos, 6-8 lr_color, 9 lr_alpha),
+ * then fit.rs:399-424 `project` when project != 0. `step` is the 1-based step
+ * count t used for bias correction (Adam::t after its increment). m and v are
+ * the caller's moment buffers. Bit-identical to the reference's f32 arithmetic. */
+DR_API dr_status dr_adam_step(dr_ctx* ctx, float* params, float* m, float* v, const float* grads,
+                       int64_t n, float lr_pos, float lr_color, float lr_alpha, uint32_t step,
+                       float beta1, float beta2, float eps, int project, dr_stream_t stream);
+
+/* FitConfig (crates/diffrast/src/fit.rs:49-89) minus triangles/seed, which
+ * come with the initial scene. patience < 0 means None. */
+typedef struct dr_fit_config {
+  int64_t iters;
+  float sigma_start, sigma_end;
+  float lr_pos, lr_color, lr_alpha;
+  int64_t patience;
+  float min_delta;
+} dr_fit_config;
+
+typedef enum dr_stop_reason {
+  DR_STOP_COMPLETED = 0,
+  DR_STOP_CONVERGED = 1,
+  DR_STOP_DIVERGED = 2
+} dr_stop_reason;
+
+/* FitReport (fit.rs:128-140). */
+typedef struct dr_fit_report {
+  int64_t n_losses;
+  int64_t best_iter;
+  float best_loss;
+  int stop_reason;
+  int config_error; /* 0, or ConfigError 1..4 (fit.rs:27-32 order) */
+} dr_fit_report;
+
+/* The whole fit loop on the device (fit.rs:166-181, Fitter::step fit.rs:243-288):
+ * per iteration sigma_at (fit.rs:343-349), fused forward+MSE+backward, the
+ * Diverged / best / patience bookkeeping, Adam and projection, all without a
+ * host round trip; synchronizes once at the end. target (H,W,3) and
+ * init_params (T,10) are device memory; background is 3 host floats (the
+ * seeded scene's background, fit.rs:357). best_params / final_params (T,10)
+ * are device outputs; losses is a HOST array of at least iters floats.
+ * An invalid config returns DR_INVALID_ARGUMENT with report->config_error set. */
+DR_API dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* init_params,
+                 const float* background, int T, const dr_fit_config* cfg, float* best_params,
+                 float* final_params, float* losses, dr_fit_report* report, dr_stream_t stream);
+
+/* --- pool / sync ---------------------------------------------------------- */
+
+/* PoolStats (diffrast-gpu/src/lib.rs:153-158): scratch reuse counters. */
+typedef struct dr_pool_stats {
+  uint64_t hits, misses, bytes;
+} dr_pool_stats;
+
+DR_API dr_status dr_pool_stats_get(dr_ctx* ctx, dr_pool_stats* out); /* lib.rs:346-349 */
+DR_API dr_status dr_clear_pool(dr_ctx* ctx);                           /* lib.rs:352-356 */
+
+/* Bounded wait for `stream`: polls and returns DR_TIMEOUT after timeout_s
+ * seconds (GpuRasterizer::POLL_TIMEOUT, diffrast-gpu/src/lib.rs:223-229). */
+DR_API dr_status dr_stream_wait(dr_stream_t stream, double timeout_s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DIFFRAST_CUDA_H */

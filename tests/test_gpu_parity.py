@@ -1,0 +1,282 @@
+"""CUDA path vs the CPU oracle (the reference's algorithm restated), on the same
+seeded inputs. Tolerances are the north star's: images |d| <= 1e-5 + 1e-4|ref|,
+gradients per element |d| <= 1e-6 + 1e-3|ref|.
+
+Every call goes through the C ABI (libdiffrast_cuda.so) via diffrast._native.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import (assert_grads_close, assert_images_close, rel_norm_error)
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def native():
+    from diffrast import _native
+
+    assert torch.cuda.is_available(), "GPU tests need CUDA"
+    return _native
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def run_all(native, oracle, params, target, sigma, bg=(0.0, 0.0, 0.0), check_grads=True,
+            slack=True):
+    """Forward, loss+backward, grad-input backward; compare each to the oracle."""
+    B, T = params.shape[:2]
+    H, W = target.shape[1], target.shape[2]
+    img = host(native.render(cuda(params), H, W, sigma, bg))
+    ref_img = oracle.render_batch(params, H, W, sigma, bg)
+    assert_images_close(img, ref_img, "render")
+
+    losses, grads, img2 = native.loss_backward(cuda(params), cuda(target), sigma, bg,
+                                               want_image=True)
+    losses, grads, img2 = host(losses), host(grads), host(img2)
+    ref_l, ref_g, ref_img2 = oracle.backward_batch(params, target, sigma, bg, want_images=True)
+    assert_images_close(img2, ref_img2, "fused render")
+    np.testing.assert_allclose(losses, ref_l, rtol=1e-5, atol=1e-9)
+    if check_grads:
+        sl = None
+        if slack:
+            _, g64 = oracle.backward_batch(params, target, sigma, bg, f64=True)
+            sl = np.abs(ref_g.astype(np.float64) - g64)
+        assert_grads_close(grads, ref_g, "loss grads", slack=sl)
+        for b in range(B):
+            assert rel_norm_error(grads[b], ref_g[b]) < 1e-3
+
+    # Upstream-gradient mode (autograd path) vs the oracle's direct variant.
+    g_in = np.random.default_rng(7).normal(0, 1e-4, size=target.shape).astype(np.float32)
+    gg = host(native.grad_backward(cuda(params), cuda(g_in), sigma, bg))
+    _, ref_gg = oracle.backward_batch(params, g_in, sigma, bg, mode=oracle.MODE_DIRECT_GRAD)
+    if check_grads:
+        sl = None
+        if slack:
+            _, g64 = oracle.backward_batch(params, g_in, sigma, bg, mode=oracle.MODE_DIRECT_GRAD,
+                                           f64=True)
+            sl = np.abs(ref_gg.astype(np.float64) - g64)
+        assert_grads_close(gg, ref_gg, "grad-input grads", slack=sl)
+    return img, grads
+
+
+def tri(verts, color, alpha):
+    return np.array(list(np.ravel(verts)) + list(color) + [alpha], dtype=np.float32)
+
+
+def test_reference_test_scenes(native, oracle):
+    # grad.rs:329-346 scene_pair at the sigmas its tests use.
+    bg = (0.1, 0.12, 0.15)
+    target_p = np.stack([
+        tri([[0.25, 0.30], [0.80, 0.22], [0.55, 0.78]], [0.9, 0.3, 0.2], 0.8),
+        tri([[0.15, 0.60], [0.70, 0.65], [0.40, 0.20]], [0.2, 0.6, 0.9], 0.6)])[None]
+    scene = np.stack([
+        tri([[0.21, 0.34], [0.77, 0.26], [0.58, 0.72]], [0.7, 0.4, 0.3], 0.7),
+        tri([[0.18, 0.55], [0.66, 0.69], [0.44, 0.24]], [0.3, 0.5, 0.8], 0.5)])[None]
+    for sigma in (0.01, 0.02, 0.03):
+        target = oracle.render_batch(target_p, 48, 48, sigma, bg)
+        run_all(native, oracle, scene, target, sigma, bg)
+
+
+def test_unit_triangle_paints_over_background(native):
+    # raster.rs:212-220 on the GPU.
+    p = np.array([[[0.2, 0.2, 0.8, 0.2, 0.5, 0.8, 1.0, 0.0, 0.0, 1.0]]], np.float32)
+    img = host(native.render(cuda(p), 64, 64, 0.002))[0]
+    assert img[25, 32, 0] > 0.99 and img[25, 32, 1] < 0.01
+    assert np.array_equal(img[63, 0], [0.0, 0.0, 0.0])
+
+
+@pytest.mark.parametrize("W,H,T", [(37, 19, 33), (8, 8, 1), (17, 41, 65), (64, 64, 32),
+                                   (96, 80, 200), (1, 1, 4), (64, 1, 8), (1, 64, 8)])
+@pytest.mark.parametrize("sigma", [0.0015, 0.01, 0.03])
+def test_seeded_scenes_match_oracle(native, oracle, W, H, T, sigma):
+    from diffrast.scenes import uniform_scenes
+
+    params = uniform_scenes(3, T, seed=W * 1000 + H * 10 + T)
+    target = oracle.render_batch(uniform_scenes(3, T, seed=17 + T), H, W, sigma, (0.2, 0.3, 0.4))
+    run_all(native, oracle, params, target, sigma, (0.05, 0.1, 0.15))
+
+
+def test_small_triangles_like_reference_benches(native, oracle):
+    # Scene::random(n, bg, 0.15) shapes (benches/raster.rs:16-19): small triangles.
+    rng = np.random.default_rng(11)
+    B, T = 4, 128
+    c = rng.uniform(0, 1, size=(B, T, 1, 2))
+    v = c + rng.uniform(-0.15, 0.15, size=(B, T, 3, 2))
+    p = np.concatenate([v.reshape(B, T, 6), rng.uniform(0, 1, (B, T, 3)),
+                        rng.uniform(0.3, 0.8, (B, T, 1))], -1).astype(np.float32)
+    target = np.full((B, 64, 64, 3), 0.3, np.float32)
+    run_all(native, oracle, p, target, 0.01, (0.5, 0.5, 0.5))
+
+
+def test_layouts_agree(native):
+    from diffrast.scenes import uniform_scenes
+
+    p = cuda(uniform_scenes(2, 40, 3))
+    a = native.render(p, 33, 47, 0.01, layout=native.LAYOUT_BHWC)
+    b = native.render(p, 33, 47, 0.01, layout=native.LAYOUT_BCHW)
+    assert torch.equal(a.permute(0, 3, 1, 2), b)
+    tgt = torch.rand(2, 33, 47, 3, device="cuda")
+    la, ga = native.loss_backward(p, tgt, 0.01, layout=native.LAYOUT_BHWC)
+    lb, gb = native.loss_backward(p, tgt.permute(0, 3, 1, 2).contiguous(), 0.01,
+                                  layout=native.LAYOUT_BCHW)
+    assert torch.equal(la, lb)
+    torch.testing.assert_close(ga, gb, rtol=1e-5, atol=1e-9)
+
+
+def test_many_triangles_span_several_bins(native, oracle):
+    # More triangles than one shared-memory chunk holds, heavily overlapping.
+    from diffrast.scenes import uniform_scenes
+
+    p = uniform_scenes(2, 700, 5, lo=0.3, hi=0.7)
+    target = oracle.render_batch(uniform_scenes(2, 50, 6), 40, 40, 0.005)
+    run_all(native, oracle, p, target, 0.005)
+
+
+def test_per_scene_backgrounds_and_order(native, oracle):
+    from diffrast.scenes import uniform_scenes
+
+    p = uniform_scenes(6, 5, 9)
+    bgs = np.array([[i / 6.0] * 3 for i in range(6)], np.float32)
+    target = np.random.default_rng(1).uniform(0, 1, (6, 16, 16, 3)).astype(np.float32)
+    run_all(native, oracle, p, target, 0.02, bgs)
+
+
+def test_empty_inputs(native):
+    p = cuda(np.zeros((0, 4, 10)))
+    assert native.render(p, 8, 8, 0.01).shape == (0, 8, 8, 3)
+    img = host(native.render(cuda(np.zeros((2, 0, 10))), 16, 16, 0.01, (0.2, 0.4, 0.6)))
+    assert np.all(img == np.array([0.2, 0.4, 0.6], np.float32))
+    tgt = np.full((2, 16, 16, 3), 0.5, np.float32)
+    l, g = native.loss_backward(cuda(np.zeros((2, 0, 10))), cuda(tgt), 0.01, (0.2, 0.4, 0.6))
+    assert g.shape == (2, 0, 10)
+    np.testing.assert_allclose(host(l), np.mean((img - 0.5) ** 2, axis=(1, 2, 3)), rtol=1e-6)
+
+
+def test_edge_case_triangles(native, oracle):
+    # Off-screen, zero / one / tiny / NaN opacity, coincident, collinear and
+    # NaN-vertex triangles in one scene.
+    rows = [
+        tri([[5.0, 5.0], [6.0, 5.0], [5.5, 6.0]], [1, 1, 1], 1.0),
+        tri([[0.1, 0.1], [0.9, 0.2], [0.4, 0.9]], [1, 0, 0], 0.0),
+        tri([[0.2, 0.1], [0.8, 0.8], [0.1, 0.7]], [0, 1, 0], 1.0),
+        tri([[0.3, 0.3], [0.6, 0.3], [0.45, 0.6]], [0, 0, 1], 5e-7),
+        tri([[0.5, 0.5], [0.5, 0.5], [0.5, 0.5]], [1, 1, 0], 0.9),
+        tri([[0.2, 0.2], [0.4, 0.4], [0.8, 0.8]], [0, 1, 1], 0.8),
+        tri([[0.2, 0.6], [0.2, 0.6], [0.9, 0.1]], [1, 0, 1], 0.7),
+        tri([[np.nan, 0.6], [0.2, 0.6], [0.9, 0.1]], [1, 0, 1], 0.7),
+        tri([[0.0, 0.0], [1.0, 0.0], [0.0, 1.0]], [0.3, 0.3, 0.3], 1.0),
+        tri([[0.3, 0.2], [0.7, 0.4], [0.5, 0.9]], [0.9, 0.1, 0.5], 0.6),
+    ]
+    p = np.stack(rows)[None]
+    target = np.random.default_rng(3).uniform(0, 1, (1, 32, 32, 3)).astype(np.float32)
+    for sigma in (0.001, 0.02):
+        run_all(native, oracle, p, target, sigma, (0.1, 0.2, 0.3))
+        _, g = oracle.backward_batch(p, target, sigma)
+        assert g[0, 2, 9] == 0.0  # alpha == 1 is pinned (grad.rs:471-481)
+
+
+def test_nan_alpha_render_vs_tape_semantics(native, oracle):
+    # raster::render paints a NaN-alpha triangle (alpha <= 0 is false) while
+    # render_with_tape drops it (alpha > 0 is false); both paths must agree.
+    p = np.stack([tri([[0.1, 0.1], [0.9, 0.2], [0.4, 0.9]], [1, 0, 0], 0.5),
+                  tri([[0.3, 0.3], [0.7, 0.3], [0.5, 0.7]], [0, 1, 0], np.nan)])[None]
+    img = host(native.render(cuda(p), 24, 24, 0.01))
+    ref = oracle.render_batch(p, 24, 24, 0.01)
+    assert np.isnan(ref).any()
+    assert_images_close(img, ref, "NaN-alpha render")
+    target = np.zeros((1, 24, 24, 3), np.float32)
+    l, g, im2 = native.loss_backward(cuda(p), cuda(target), 0.01, want_image=True)
+    rl, rg, rim = oracle.backward_batch(p, target, 0.01, want_images=True)
+    assert not np.isnan(rim).any()
+    assert_images_close(host(im2), rim, "NaN-alpha taped render")
+    assert_grads_close(host(g), rg)
+
+
+@pytest.mark.parametrize("sigma", [0.00015, 0.0015, 0.015])
+def test_config5_stress(native, oracle, sigma):
+    from diffrast.scenes import config5_params
+
+    p = config5_params(2, 2048, 5000)
+    target = oracle.render_batch(config5_params(2, 2048, 5100), 512, 512, sigma)
+    img, grads = run_all(native, oracle, p, target, sigma)
+    assert np.isfinite(img).all() and np.isfinite(grads).all()
+    zero_alpha = p[..., 9] == 0.0
+    assert np.all(grads[zero_alpha] == 0.0)
+    one_alpha = p[..., 9] == 1.0
+    assert np.all(grads[one_alpha][:, 9] == 0.0)
+
+
+def test_config4_large_scene(native, oracle):
+    from diffrast.scenes import config4_params
+
+    p = config4_params(4096, 4000)
+    target = oracle.render_batch(config4_params(4096, 4001), 1024, 1024, 0.0015)
+    run_all(native, oracle, p, target, 0.0015)
+
+
+@pytest.mark.parametrize("T", [32, 128, 512])
+@pytest.mark.parametrize("size", [64, 128, 256])
+def test_config2_cells(native, oracle, T, size):
+    from diffrast.scenes import config2_params
+
+    cell = [32, 128, 512].index(T) * 3 + [64, 128, 256].index(size)
+    p, tp = config2_params(4, T, cell)
+    target = oracle.render_batch(tp, size, size, 0.0015)
+    run_all(native, oracle, p, target, 0.0015)
+
+
+def test_headline_batch_properties(native):
+    # Full B=32, T=128, 256^2: the batch result equals each scene run alone,
+    # and the fused loss equals the MSE of the fused render.
+    from diffrast.scenes import config2_params
+
+    p, tp = config2_params(32, 128, 5)
+    P, TP = cuda(p), cuda(tp)
+    tgt = native.render(TP, 256, 256, 0.0015)
+    losses, grads, img = native.loss_backward(P, tgt, 0.0015, want_image=True)
+    for b in (0, 17, 31):
+        lb, gb, ib = native.loss_backward(P[b:b + 1], tgt[b:b + 1], 0.0015, want_image=True)
+        assert torch.equal(ib[0], img[b])
+        assert lb[0].item() == losses[b].item()
+        torch.testing.assert_close(gb[0], grads[b], rtol=1e-5, atol=1e-9)
+    mse = ((img.double() - tgt.double()) ** 2).flatten(1).mean(1)
+    torch.testing.assert_close(losses.double(), mse, rtol=1e-6, atol=0)
+    assert torch.isfinite(grads).all()
+
+
+def test_mse_kernel_matches_oracle(native, oracle):
+    rng = np.random.default_rng(0)
+    a = rng.uniform(0, 1, (3, 192, 192, 3)).astype(np.float32)
+    b = rng.uniform(0, 1, (3, 192, 192, 3)).astype(np.float32)
+    got = host(native.mse_loss(cuda(a), cuda(b)))
+    for i in range(3):
+        assert abs(got[i] - oracle.mse(a[i], b[i])) <= 1e-7 * abs(got[i])
+
+
+def test_adam_is_bit_exact(native, oracle):
+    rng = np.random.default_rng(4)
+    n = 10 * 97
+    p0 = rng.uniform(-0.5, 1.5, n).astype(np.float32)
+    p0[5] = np.nan
+    lr = oracle.learning_rates(97)
+    adam = oracle.Adam(n)
+    p_ref = p0.copy()
+    P, M, V = cuda(p0), torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    for step in range(1, 30):
+        g = rng.normal(0, 1e-2, n).astype(np.float32)
+        adam.step(p_ref, g, lr)
+        oracle.project(p_ref)
+        native.adam_step(P, M, V, cuda(g), step)
+        assert np.array_equal(host(P), p_ref, equal_nan=True), step
