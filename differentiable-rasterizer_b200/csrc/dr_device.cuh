@@ -38,7 +38,7 @@ struct __align__(16) TriRec {
   float c[3];     // edge line offsets: l_i(p) = n_i . p + c_i
   int bbox[4];    // x0 y0 x1 y1 of pixel_bounds (raster.rs:144-168)
   int flags;
-  int pad[3];
+  float il[3];    // 1 / len2 (0 when len2 <= 1e-20: t = 0, raster.rs:129-130)
 };
 static_assert(sizeof(TriRec) == 160, "TriRec layout");
 constexpr int kRecWords = 40;
@@ -47,12 +47,6 @@ enum RecFlags : int {
   kLive = 1,         // has a non-empty box and a usable alpha
   kAlphaActive = 2,  // 0 < raw alpha < 1: alpha receives gradient (grad.rs:145)
   kFastOk = 4,       // non-degenerate, finite alpha: edge-line tests are valid
-};
-
-// List-entry flags decided per (tile, triangle) while binning.
-enum EntryFlags : int {
-  kBoxCoversTile = 1,  // every pixel of the tile lies in the triangle's box
-  kTileInside = 2,     // every pixel of the tile is deep inside: w == alpha
 };
 
 // f32::clamp (NaN passes through).

@@ -29,9 +29,10 @@
 namespace dr {
 
 constexpr int kTile = 16;
-constexpr int kThreads = 256;
-constexpr int kChunk = 128;  // triangles binned per round (<= kThreads)
-constexpr int kWarps = kThreads / 32;
+constexpr int kPPT = 2;                                  // pixels per thread
+constexpr int kWarps = 4;                                // 8x8 warp blocks per tile
+constexpr int kThreads = kWarps * 32;
+constexpr int kChunk = kThreads;                         // triangles binned per round
 constexpr float kRenorm = 18446744073709551616.0f;        // 2^64
 constexpr float kRenormInv = 5.42101086242752217e-20f;    // 2^-64
 
@@ -144,9 +145,9 @@ __global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W,
   // Slack for evaluating n.p + c in f32 and for the reference's own f32
   // distance rounding: a few ulps of the largest magnitude involved.
   r.margin = (float)(4e-6 * (2.0 + maxabs));
+  for (int k = 0; k < 3; ++k) r.il[k] = r.len2[k] <= 1e-20f ? 0.0f : (float)(1.0 / (double)r.len2[k]);
   if (fast) flags |= kFastOk;
   r.flags = flags;
-  r.pad[0] = r.pad[1] = r.pad[2] = 0;
 
   float4* dst = reinterpret_cast<float4*>(recs + i);
   const float4* src = reinterpret_cast<const float4*>(&r);
@@ -157,10 +158,25 @@ __global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W,
 // ---------------------------------------------------------------------------
 // Raster kernel
 // ---------------------------------------------------------------------------
+//
+// One CTA per (scene, 16x16 tile), 4 warps; each warp owns an 8x8 block and
+// each lane two pixels of it (rows y and y + 4). Triangles are binned per
+// tile in order (build_list) and every kept (tile, triangle) entry carries a
+// 4-bit code per warp block, decided once at binning time from the block's
+// rectangle against the triangle's box and edge lines:
+//   kBlkSkip    no pixel of the block can contribute (outside the box, or
+//               every pixel more than kRejectSigmas outside an edge line)
+//   kBlkBox     the block straddles the box: test each pixel against it
+//   kBlkInside  every pixel is more than kAcceptSigmas inside every edge:
+//               w == alpha exactly, no geometry
+// so whole warps skip or take the cheap path on a uniform branch.
+
+constexpr int kBlkSkip = 1, kBlkBox = 2, kBlkInside = 4;
+constexpr int kBlockW = 8, kBlockH = 4 * kPPT;
 
 struct Smem {
   TriRec rec[kChunk];
-  int eflags[kChunk];
+  int bcode[kChunk];
   int kidx[kChunk];
   float acc[kChunk][kParams];
   int warp_count[kWarps];
@@ -168,58 +184,70 @@ struct Smem {
   int is_last;
 };
 
-// Bin triangles [c0, c0 + kChunk) of scene b against tile [tx0,tx1)x[ty0,ty1)
-// into shared memory, preserving triangle order. Returns the entry count.
-__device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int c0, int tx0,
-                          int ty0, int tx1, int ty1, int W, int H, float rej, float acc) {
-  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int k = c0 + (int)threadIdx.x;
-  bool keep = false;
-  int ef = 0;
-  const TriRec* r = recs + k;
-  if ((int)threadIdx.x < kChunk && k < T) {
-    int flags = r->flags;
-    int bx0 = r->bbox[0], by0 = r->bbox[1], bx1 = r->bbox[2], by1 = r->bbox[3];
-    keep = (flags & kLive) && bx0 < tx1 && bx1 > tx0 && by0 < ty1 && by1 > ty0;
-    if (keep) {
-      if (bx0 <= tx0 && bx1 >= tx1 && by0 <= ty0 && by1 >= ty1) ef |= kBoxCoversTile;
-      if (flags & kFastOk) {
-        float cx0 = pixel_center(tx0, W), cx1 = pixel_center(tx1 - 1, W);
-        float cy0 = pixel_center(ty0, H), cy1 = pixel_center(ty1 - 1, H);
-        float m = r->margin;
-        float mn_all = __int_as_float(0x7f800000);
-        bool far_out = false;
+// Block code of one warp block [bx0,bx1) x [by0,by1) (clipped to the image)
+// for one triangle record.
+__device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0, int bx1, int by1,
+                                              int W, int H, float rej, float acc) {
+  if (bx0 >= bx1 || by0 >= by1) return kBlkSkip;
+  const int x0 = r.bbox[0], y0 = r.bbox[1], x1 = r.bbox[2], y1 = r.bbox[3];
+  if (bx1 <= x0 || bx0 >= x1 || by1 <= y0 || by0 >= y1) return kBlkSkip;
+  int code = (x0 <= bx0 && x1 >= bx1 && y0 <= by0 && y1 >= by1) ? 0 : kBlkBox;
+  if (r.flags & kFastOk) {
+    // Pixel centres of the block span [c - h, c + h] per axis; a linear
+    // function's extremes over the rectangle are at l(c) +- (|nx| hx + |ny| hy).
+    const float inv_w = 1.0f / (float)W, inv_h = 1.0f / (float)H;
+    const float cx = 0.5f * (float)(bx0 + bx1) * inv_w, hx = 0.5f * (float)(bx1 - bx0 - 1) * inv_w;
+    const float cy = 0.5f * (float)(by0 + by1) * inv_h, hy = 0.5f * (float)(by1 - by0 - 1) * inv_h;
+    const float m = r.margin;
+    float lmin_all = __int_as_float(0x7f800000);
 #pragma unroll
-        for (int e = 0; e < 3; ++e) {
-          float nx = r->n[2 * e], ny = r->n[2 * e + 1], c = r->c[e];
-          float l00 = __fmaf_rn(nx, cx0, __fmaf_rn(ny, cy0, c));
-          float l10 = __fmaf_rn(nx, cx1, __fmaf_rn(ny, cy0, c));
-          float l01 = __fmaf_rn(nx, cx0, __fmaf_rn(ny, cy1, c));
-          float l11 = __fmaf_rn(nx, cx1, __fmaf_rn(ny, cy1, c));
-          float lmax = fmaxf(fmaxf(l00, l10), fmaxf(l01, l11));
-          float lmin = fminf(fminf(l00, l10), fminf(l01, l11));
-          if (lmax < -(rej + m)) far_out = true;
-          mn_all = fminf(mn_all, lmin);
-        }
-        if (far_out) keep = false;
-        if (mn_all > acc + m) ef |= kTileInside;
-      }
+    for (int e = 0; e < 3; ++e) {
+      const float nx = r.n[2 * e], ny = r.n[2 * e + 1];
+      const float lc = __fmaf_rn(nx, cx, __fmaf_rn(ny, cy, r.c[e]));
+      const float rad = __fmaf_rn(fabsf(nx), hx, __fmul_rn(fabsf(ny), hy));
+      if (__fadd_rn(lc, rad) < -(rej + m)) return kBlkSkip;
+      lmin_all = fminf(lmin_all, __fsub_rn(lc, rad));
     }
+    if (lmin_all > acc + m) code = kBlkInside;  // deep inside implies inside the box
   }
-  unsigned ballot = __ballot_sync(0xffffffffu, keep);
+  return code;
+}
+
+// Bin triangles [c0, c0 + kChunk) of one scene against the tile, in order.
+__device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int c0, int tx0,
+                          int ty0, int W, int H, float rej, float acc) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int k = c0 + (int)threadIdx.x;
+  bool keep = false;
+  int code_all = 0;
+  const TriRec* r = recs + k;
+  if ((int)threadIdx.x < kChunk && k < T && (r->flags & kLive)) {
+    const TriRec& rr = *r;
+    int skipped = 0;
+#pragma unroll
+    for (int wb = 0; wb < kWarps; ++wb) {
+      const int bx0 = tx0 + (wb & 1) * kBlockW, by0 = ty0 + (wb >> 1) * kBlockH;
+      const int c = classify_block(rr, bx0, by0, min(bx0 + kBlockW, W), min(by0 + kBlockH, H), W,
+                                   H, rej, acc);
+      code_all |= c << (4 * wb);
+      skipped += (c & kBlkSkip) ? 1 : 0;
+    }
+    keep = skipped < kWarps;
+  }
+  const unsigned ballot = __ballot_sync(0xffffffffu, keep);
   if (lane == 0) sm.warp_count[warp] = __popc(ballot);
   __syncthreads();
   int base = 0, total = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) {
-    int cnt = sm.warp_count[w];
+    const int cnt = sm.warp_count[w];
     base += (w < warp) ? cnt : 0;
     total += cnt;
   }
   if (keep) {
-    int slot = base + __popc(ballot & ((1u << lane) - 1u));
+    const int slot = base + __popc(ballot & ((1u << lane) - 1u));
     sm.kidx[slot] = k;
-    sm.eflags[slot] = ef;
+    sm.bcode[slot] = code_all;
     const float4* src = reinterpret_cast<const float4*>(r);
     float4* dst = reinterpret_cast<float4*>(&sm.rec[slot]);
 #pragma unroll
@@ -229,47 +257,136 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
   return total;
 }
 
-// Per-pixel evaluation of one list entry: returns true when the pair
-// contributes (w > MIN_WEIGHT) and fills w, cov and (if want_geo) the
-// nearest-edge data. Mirrors raster.rs:53-59 with the box test of
-// raster.rs:144-168 and the conservative fast paths described in
-// dr_device.cuh.
-struct PairEval {
-  float w, cov;
-  bool band;  // full geometry evaluated (else cov == 1 exactly)
-  SdResult g;
+struct Consts {
+  float sigma_eff, inv_sigma, rej, acc;
 };
 
-__device__ __forceinline__ bool eval_pair(const TriRec& r, int ef, int px, int py, float ptx,
-                                          float pty, float sigma_eff, float rej, float acc,
-                                          PairEval& out) {
-  if (!(ef & kBoxCoversTile)) {
+// What one (pixel, triangle) pair contributes. `band` means the coverage
+// came from the full geometry (else cov == 1 exactly). The gradient fields
+// are filled only when kGrad.
+struct PairEval {
+  float w, cov;
+  bool band, inside;
+  float dist, t, ux, uy;
+  int edge;
+};
+
+// raster.rs:96-106 sigmoid of the signed distance, fast form: one ex2 and one
+// rcp on the MUFU pipe. Same branch structure as raster.rs:79-87.
+__device__ __forceinline__ float sigmoid_fast(float x) {
+  const float e = __expf(-fabsf(x));
+  const float r = __fdividef(1.0f, __fadd_rn(1.0f, e));
+  return x >= 0.0f ? r : __fmul_rn(e, r);
+}
+
+// Exact reference arithmetic for one pair (degenerate triangles, NaN alpha,
+// and every band pair in strict mode): raster.rs:96-106 + grad.rs:231-270.
+template <bool kGrad>
+__device__ __forceinline__ bool eval_ref(const TriRec& r, float ptx, float pty, const Consts& K,
+                                         PairEval& o) {
+  const SdResult g = signed_distance_ref(r.v, r.e, r.len2, ptx, pty);
+  o.cov = sigmoid_ref(__fdiv_rn(g.sd, K.sigma_eff));
+  o.w = __fmul_rn(r.alpha, o.cov);
+  o.band = true;
+  o.inside = g.sd > 0.0f;
+  if (kGrad) {
+    o.dist = g.dist;
+    o.t = g.t;
+    o.edge = g.edge;
+    const float ax = r.v[2 * g.edge], ay = r.v[2 * g.edge + 1];
+    const float cpx = __fadd_rn(ax, __fmul_rn(g.t, r.e[2 * g.edge]));
+    const float cpy = __fadd_rn(ay, __fmul_rn(g.t, r.e[2 * g.edge + 1]));
+    o.ux = __fdiv_rn(__fsub_rn(ptx, cpx), g.dist);
+    o.uy = __fdiv_rn(__fsub_rn(pty, cpy), g.dist);
+  }
+  return !(o.w <= kMinWeight);
+}
+
+// One pair, given the warp block's code. Returns true when the pair
+// composites (w > MIN_WEIGHT). The arithmetic that decides w uses explicit
+// rounding intrinsics only, so the forward pass and the gradient pass (two
+// instantiations) compute bit-identical w.
+template <bool kGrad, bool kStrict>
+__device__ __forceinline__ bool eval_pair(const TriRec& r, int code, int px, int py, float ptx,
+                                          float pty, const Consts& K, PairEval& o) {
+  if (code & kBlkBox) {
     if (px < r.bbox[0] || px >= r.bbox[2] || py < r.bbox[1] || py >= r.bbox[3]) return false;
   }
-  if (ef & kTileInside) {
-    out.cov = 1.0f;
-    out.w = r.alpha;
-    out.band = false;
+  if (code & kBlkInside) {
+    o.cov = 1.0f;
+    o.w = r.alpha;
+    o.band = false;
     return true;  // alpha > MIN_WEIGHT is guaranteed by the set-up cull
   }
-  if (r.flags & kFastOk) {
-    float l0 = __fmaf_rn(r.n[0], ptx, __fmaf_rn(r.n[1], pty, r.c[0]));
-    float l1 = __fmaf_rn(r.n[2], ptx, __fmaf_rn(r.n[3], pty, r.c[1]));
-    float l2 = __fmaf_rn(r.n[4], ptx, __fmaf_rn(r.n[5], pty, r.c[2]));
-    float mn = fminf(fminf(l0, l1), l2);
-    if (mn < -(rej + r.margin)) return false;
-    if (mn > acc + r.margin) {
-      out.cov = 1.0f;
-      out.w = r.alpha;
-      out.band = false;
-      return true;
+  if (!(r.flags & kFastOk)) return eval_ref<kGrad>(r, ptx, pty, K, o);
+  const float l0 = __fmaf_rn(r.n[0], ptx, __fmaf_rn(r.n[1], pty, r.c[0]));
+  const float l1 = __fmaf_rn(r.n[2], ptx, __fmaf_rn(r.n[3], pty, r.c[1]));
+  const float l2 = __fmaf_rn(r.n[4], ptx, __fmaf_rn(r.n[5], pty, r.c[2]));
+  const float mn = fminf(fminf(l0, l1), l2);
+  if (mn < -(K.rej + r.margin)) return false;
+  if (mn > K.acc + r.margin) {
+    o.cov = 1.0f;
+    o.w = r.alpha;
+    o.band = false;
+    return true;
+  }
+  if (kStrict) return eval_ref<kGrad>(r, ptx, pty, K, o);
+  // Inside a convex polygon the nearest boundary point is the foot on the
+  // nearest edge line, so the distance is min_i l_i and the direction from it
+  // is that edge's inward normal. Outside, the distance is the smallest
+  // clamped segment distance (raster.rs:124-134).
+  const bool inside = mn >= 0.0f;
+  float dist, t = 0.0f, ux = 0.0f, uy = 0.0f;
+  int edge = 0;
+  if (inside) {
+    dist = mn;
+    if (kGrad) {
+      float best = l0;
+      if (l1 < best) { best = l1; edge = 1; }
+      if (l2 < best) { edge = 2; }
+      const float ex = r.e[2 * edge], ey = r.e[2 * edge + 1];
+      const float apx = __fsub_rn(ptx, r.v[2 * edge]), apy = __fsub_rn(pty, r.v[2 * edge + 1]);
+      t = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[edge]));
+      ux = r.n[2 * edge];
+      uy = r.n[2 * edge + 1];
+    }
+  } else {
+    float bd2 = __int_as_float(0x7f800000), bdx = 0.0f, bdy = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 3; ++e) {
+      const float ex = r.e[2 * e], ey = r.e[2 * e + 1];
+      const float apx = __fsub_rn(ptx, r.v[2 * e]), apy = __fsub_rn(pty, r.v[2 * e + 1]);
+      const float te = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[e]));
+      const float dx = __fmaf_rn(-te, ex, apx), dy = __fmaf_rn(-te, ey, apy);
+      const float d2 = __fmaf_rn(dx, dx, __fmul_rn(dy, dy));
+      if (d2 < bd2) {
+        bd2 = d2;
+        bdx = dx;
+        bdy = dy;
+        t = te;
+        edge = e;
+      }
+    }
+    const float rs = rsqrtf(bd2);
+    dist = bd2 > 0.0f ? __fmul_rn(bd2, rs) : 0.0f;
+    if (kGrad) {
+      ux = __fmul_rn(bdx, rs);
+      uy = __fmul_rn(bdy, rs);
     }
   }
-  out.g = signed_distance_ref(r.v, r.e, r.len2, ptx, pty);
-  out.cov = sigmoid_ref(__fdiv_rn(out.g.sd, sigma_eff));
-  out.w = __fmul_rn(r.alpha, out.cov);
-  out.band = true;
-  return !(out.w <= kMinWeight);
+  const float x = __fmul_rn(inside ? dist : -dist, K.inv_sigma);
+  o.cov = sigmoid_fast(x);
+  o.w = __fmul_rn(r.alpha, o.cov);
+  o.band = true;
+  o.inside = inside && dist > 0.0f;
+  if (kGrad) {
+    o.dist = dist;
+    o.t = t;
+    o.edge = edge;
+    o.ux = ux;
+    o.uy = uy;
+  }
+  return !(o.w <= kMinWeight);
 }
 
 // Running product of (1 - w) with 2^64 renormalisation and barrier tracking.
@@ -303,28 +420,92 @@ struct Prod {
   }
 };
 
-// A_k = prod over layers above k of (1 - w), given the full product P (after
-// the last layer) and the running product Q (through layer k).
+// A_k = prod over layers above k of (1 - w), from the full product P (after
+// the last layer) and the running product Q (through layer k). A barrier
+// layer resets Q to 1, so the same ratio yields the product above it.
+template <bool kStrict>
 __device__ __forceinline__ float attenuation(const Prod& P, const Prod& Q, int k) {
   if (k < P.zn) return __int_as_float(0x7fc00000);
   if (k < P.z0) return 0.0f;
-  float ratio = __fdiv_rn(P.m, Q.m);
-  int de = P.e - Q.e;
+  const float ratio = kStrict ? __fdiv_rn(P.m, Q.m) : __fdividef(P.m, Q.m);
+  const int de = P.e - Q.e;
   if (de == 0) return ratio;
   if (de == 1) return __fmul_rn(ratio, kRenormInv);
   if (de == 2) return __fmul_rn(__fmul_rn(ratio, kRenormInv), kRenormInv);
   return 0.0f;
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// Transposed warp reduction of 10 per-lane values: each halving step keeps
+// half of the values and trades the other half with the partner lane, so the
+// 10 warp totals cost 12 shuffles instead of 50. On return, lane `slot`
+// (see reduce10_slot) holds the total of value `slot`'s index.
+__device__ __forceinline__ float reduce10(const float (&v)[10], int lane) {
+  const unsigned F = 0xffffffffu;
+  bool h = lane & 16;
+  float a[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const float keep = h ? v[5 + i] : v[i];
+    const float send = h ? v[i] : v[5 + i];
+    a[i] = keep + __shfl_xor_sync(F, send, 16);
+  }
+  h = lane & 8;
+  float b0, b1, b2;
+  {
+    const float k0 = h ? a[3] : a[0], s0 = h ? a[0] : a[3];
+    const float k1 = h ? a[4] : a[1], s1 = h ? a[1] : a[4];
+    const float k2 = h ? 0.0f : a[2], s2 = h ? a[2] : 0.0f;
+    b0 = k0 + __shfl_xor_sync(F, s0, 8);
+    b1 = k1 + __shfl_xor_sync(F, s1, 8);
+    b2 = k2 + __shfl_xor_sync(F, s2, 8);
+  }
+  h = lane & 4;
+  float c0, c1;
+  {
+    const float k0 = h ? b2 : b0, s0 = h ? b0 : b2;
+    const float k1 = h ? 0.0f : b1, s1 = h ? b1 : 0.0f;
+    c0 = k0 + __shfl_xor_sync(F, s0, 4);
+    c1 = k1 + __shfl_xor_sync(F, s1, 4);
+  }
+  h = lane & 2;
+  const float k = h ? c1 : c0, s = h ? c0 : c1;
+  float d = k + __shfl_xor_sync(F, s, 2);
+  d += __shfl_xor_sync(F, d, 1);
+  return d;
+}
+
+// The value index lane `lane` holds after reduce10, or -1.
+__device__ __forceinline__ int reduce10_slot(int lane) {
+  if (lane & 1) return -1;
+  const int b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1, b1 = (lane >> 1) & 1;
+  const int pos = b2 ? (b1 ? -1 : 2) : b1;  // position among the 3 kept after step 2
+  if (pos < 0) return -1;
+  const int local = b3 ? (pos < 2 ? 3 + pos : -1) : pos;
+  return local < 0 ? -1 : 5 * b4 + local;
+}
+
+// 4 values (colour and alpha gradients): lane 8*i holds the total of v[i].
+__device__ __forceinline__ float reduce4(float v0, float v1, float v2, float v3, int lane) {
+  const unsigned F = 0xffffffffu;
+  bool h = lane & 16;
+  float k0 = h ? v2 : v0, s0 = h ? v0 : v2;
+  float k1 = h ? v3 : v1, s1 = h ? v1 : v3;
+  k0 += __shfl_xor_sync(F, s0, 16);
+  k1 += __shfl_xor_sync(F, s1, 16);
+  h = lane & 8;
+  float k = h ? k1 : k0;
+  const float s = h ? k0 : k1;
+  k += __shfl_xor_sync(F, s, 8);
+  k += __shfl_xor_sync(F, k, 4);
+  k += __shfl_xor_sync(F, k, 2);
+  k += __shfl_xor_sync(F, k, 1);
+  return k;
 }
 
 __device__ __forceinline__ size_t pix_index(int layout, int b, int ch, int px, int py, int W,
@@ -333,7 +514,7 @@ __device__ __forceinline__ size_t pix_index(int layout, int b, int ch, int px, i
   return (((size_t)b * H + py) * W + px) * 3 + ch;
 }
 
-template <int Mode>
+template <int Mode, bool kStrict>
 __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -344,14 +525,19 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
   const int tile_col = local_tile % a.tiles_x;
   const int tile_row = a.tile_row0 + (local_tile / a.tiles_x) * a.tile_row_step;
   const int tx0 = tile_col * kTile, ty0 = tile_row * kTile;
-  const int tx1 = min(tx0 + kTile, a.W), ty1 = min(ty0 + kTile, a.H);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // Each warp covers an 8x4 block of the 16x16 tile.
-  const int px = tx0 + (warp & 1) * 8 + (lane & 7);
-  const int py = ty0 + (warp >> 1) * 4 + (lane >> 3);
-  const bool active = px < a.W && py < a.H;
-  const float ptx = pixel_center(px, a.W), pty = pixel_center(py, a.H);
+  const int px = tx0 + (warp & 1) * kBlockW + (lane & 7);
+  int py[kPPT];
+  bool active[kPPT];
+  float pty[kPPT];
+#pragma unroll
+  for (int q = 0; q < kPPT; ++q) {
+    py[q] = ty0 + (warp >> 1) * kBlockH + (lane >> 3) + 4 * q;
+    active[q] = px < a.W && py[q] < a.H;
+    pty[q] = pixel_center(py[q], a.H);
+  }
+  const float ptx = pixel_center(px, a.W);
 
   const TriRec* recs = a.recs + (size_t)b * a.T;
   float bg0 = a.bg3[0], bg1 = a.bg3[1], bg2 = a.bg3[2];
@@ -361,156 +547,169 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
     bg1 = q[1];
     bg2 = q[2];
   }
-  const float sig = a.sigma_eff;
-  const float rej = a.rej, acc = a.acc;
+  Consts K;
+  K.sigma_eff = a.sigma_eff;
+  K.inv_sigma = a.inv_sigma;
+  K.rej = a.rej;
+  K.acc = a.acc;
   const int n_chunks = (a.T + kChunk - 1) / kChunk;
+  const int shift = 4 * warp;
 
   // ---- pass 1: forward composite ------------------------------------------
-  float c0 = bg0, c1 = bg1, c2 = bg2;
-  Prod P;
-  P.init();
+  float c0[kPPT], c1[kPPT], c2[kPPT];
+  Prod P[kPPT];
+#pragma unroll
+  for (int q = 0; q < kPPT; ++q) {
+    c0[q] = bg0;
+    c1[q] = bg1;
+    c2[q] = bg2;
+    P[q].init();
+  }
   int count = 0;
   for (int ci = 0; ci < n_chunks; ++ci) {
-    count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, tx1, ty1, a.W, a.H, rej, acc);
-    if (active) {
-      for (int j = 0; j < count; ++j) {
-        const TriRec& r = sm.rec[j];
+    count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H, K.rej, K.acc);
+    for (int j = 0; j < count; ++j) {
+      const int code = (sm.bcode[j] >> shift) & 15;
+      if (code & kBlkSkip) continue;
+      const TriRec& r = sm.rec[j];
+      const int k = sm.kidx[j];
+#pragma unroll
+      for (int q = 0; q < kPPT; ++q) {
         PairEval pe;
-        if (!eval_pair(r, sm.eflags[j], px, py, ptx, pty, sig, rej, acc, pe)) continue;
-        float w = pe.w, om = __fsub_rn(1.0f, w);
-        c0 = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(c0, om));
-        c1 = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(c1, om));
-        c2 = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(c2, om));
-        if (Mode != kModeRender) P.mul(om, sm.kidx[j]);
+        if (!active[q] || !eval_pair<false, kStrict>(r, code, px, py[q], ptx, pty[q], K, pe))
+          continue;
+        const float w = pe.w, om = __fsub_rn(1.0f, w);
+        c0[q] = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(c0[q], om));  // raster.rs:63
+        c1[q] = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(c1[q], om));
+        c2[q] = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(c2[q], om));
+        if (Mode != kModeRender) P[q].mul(om, k);
       }
     }
-    if (ci + 1 < n_chunks) __syncthreads();
   }
 
-  if (a.image && active) {
-    a.image[pix_index(a.layout, b, 0, px, py, a.W, a.H)] = c0;
-    a.image[pix_index(a.layout, b, 1, px, py, a.W, a.H)] = c1;
-    a.image[pix_index(a.layout, b, 2, px, py, a.W, a.H)] = c2;
+  if (a.image) {
+#pragma unroll
+    for (int q = 0; q < kPPT; ++q) {
+      if (!active[q]) continue;
+      a.image[pix_index(a.layout, b, 0, px, py[q], a.W, a.H)] = c0[q];
+      a.image[pix_index(a.layout, b, 1, px, py[q], a.W, a.H)] = c1[q];
+      a.image[pix_index(a.layout, b, 2, px, py[q], a.W, a.H)] = c2[q];
+    }
   }
   if (Mode == kModeRender) return;
 
   // ---- loss and the gradient reaching the top of the stack ----------------
-  float G0 = 0.f, G1 = 0.f, G2 = 0.f;
+  float G0[kPPT], G1[kPPT], G2[kPPT];
   double sq = 0.0;
-  if (active) {
-    float o0 = a.other[pix_index(a.layout, b, 0, px, py, a.W, a.H)];
-    float o1 = a.other[pix_index(a.layout, b, 1, px, py, a.W, a.H)];
-    float o2 = a.other[pix_index(a.layout, b, 2, px, py, a.W, a.H)];
+#pragma unroll
+  for (int q = 0; q < kPPT; ++q) {
+    G0[q] = G1[q] = G2[q] = 0.0f;
+    if (!active[q]) continue;
+    const float o0 = a.other[pix_index(a.layout, b, 0, px, py[q], a.W, a.H)];
+    const float o1 = a.other[pix_index(a.layout, b, 1, px, py[q], a.W, a.H)];
+    const float o2 = a.other[pix_index(a.layout, b, 2, px, py[q], a.W, a.H)];
     if (Mode == kModeLoss) {
-      float d0 = __fsub_rn(c0, o0), d1 = __fsub_rn(c1, o1), d2 = __fsub_rn(c2, o2);
-      sq = (double)d0 * d0 + (double)d1 * d1 + (double)d2 * d2;
-      G0 = __fmul_rn(a.grad_scale, d0);  // grad.rs:112-114
-      G1 = __fmul_rn(a.grad_scale, d1);
-      G2 = __fmul_rn(a.grad_scale, d2);
+      const float d0 = __fsub_rn(c0[q], o0), d1 = __fsub_rn(c1[q], o1), d2 = __fsub_rn(c2[q], o2);
+      sq += (double)d0 * d0 + (double)d1 * d1 + (double)d2 * d2;
+      G0[q] = __fmul_rn(a.grad_scale, d0);  // grad.rs:112-114
+      G1[q] = __fmul_rn(a.grad_scale, d1);
+      G2[q] = __fmul_rn(a.grad_scale, d2);
     } else {
-      G0 = o0;
-      G1 = o1;
-      G2 = o2;
+      G0[q] = o0;
+      G1[q] = o1;
+      G2[q] = o2;
     }
   }
   if (Mode == kModeLoss) {
-    double ws = warp_sum_d(sq);
+    const double ws = warp_sum_d(sq);
     if (lane == 0) sm.loss_part[warp] = ws;
-    // published after the next __syncthreads (inside build_list / below)
   }
 
   // ---- pass 2: recomposite in forward order and accumulate gradients ------
-  float r0 = bg0, r1 = bg1, r2 = bg2;
-  Prod Q;
-  Q.init();
+  const int slot10 = reduce10_slot(lane);
+  float r0[kPPT], r1[kPPT], r2[kPPT];
+  Prod Q[kPPT];
+#pragma unroll
+  for (int q = 0; q < kPPT; ++q) {
+    r0[q] = bg0;
+    r1[q] = bg1;
+    r2[q] = bg2;
+    Q[q].init();
+  }
   for (int ci = 0; ci < n_chunks; ++ci) {
     if (n_chunks > 1) {
       __syncthreads();
-      count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, tx1, ty1, a.W, a.H, rej, acc);
+      count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H, K.rej, K.acc);
     }
     for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
     __syncthreads();
     for (int j = 0; j < count; ++j) {
+      const int code = (sm.bcode[j] >> shift) & 15;
+      if (code & kBlkSkip) continue;
       const TriRec& r = sm.rec[j];
-      const int ef = sm.eflags[j];
       const int k = sm.kidx[j];
-      float gc0 = 0.f, gc1 = 0.f, gc2 = 0.f, ga = 0.f;
-      float gv[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      bool contrib = false;
-      if (active) {
+      float acc[10];
+#pragma unroll
+      for (int i = 0; i < 10; ++i) acc[i] = 0.0f;
+      bool contrib = false, band = false;
+#pragma unroll
+      for (int q = 0; q < kPPT; ++q) {
         PairEval pe;
-        if (eval_pair(r, ef, px, py, ptx, pty, sig, rej, acc, pe)) {
-          contrib = true;
-          float w = pe.w, om = __fsub_rn(1.0f, w);
-          // A barrier layer resets Q to 1, so the same ratio yields the
-          // product of the layers above it.
-          Q.mul(om, k);
-          const float A = attenuation(P, Q, k);
-          float g0 = __fmul_rn(G0, A), g1 = __fmul_rn(G1, A), g2 = __fmul_rn(G2, A);
-          // grad.rs:162-179
-          gc0 = __fmul_rn(g0, w);
-          gc1 = __fmul_rn(g1, w);
-          gc2 = __fmul_rn(g2, w);
-          float d_w = __fmul_rn(g0, __fsub_rn(r.color[0], r0));
-          d_w = __fadd_rn(d_w, __fmul_rn(g1, __fsub_rn(r.color[1], r1)));
-          d_w = __fadd_rn(d_w, __fmul_rn(g2, __fsub_rn(r.color[2], r2)));
-          if (r.flags & kAlphaActive) ga = __fmul_rn(d_w, pe.cov);
-          float d_cov = __fmul_rn(d_w, r.alpha);
-          // coverage_with_grad (grad.rs:231-270): zero when cov == 1 exactly
-          // (fast path) or dist < 1e-9; d_cov * 0 keeps NaN propagation.
-          float coef[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          if (pe.band && !(pe.g.dist < 1e-9f)) {
-            const float cov = pe.cov, t = pe.g.t, dist = pe.g.dist;
-            const int ea = pe.g.edge, eb = (ea + 1) % 3;
-            const float ax = r.v[2 * ea], ay = r.v[2 * ea + 1];
-            const float cpx = __fadd_rn(ax, __fmul_rn(t, r.e[2 * ea]));
-            const float cpy = __fadd_rn(ay, __fmul_rn(t, r.e[2 * ea + 1]));
-            const float ux = __fdiv_rn(__fsub_rn(ptx, cpx), dist);
-            const float uy = __fdiv_rn(__fsub_rn(pty, cpy), dist);
-            const float sign = (pe.g.sd > 0.0f) ? 1.0f : -1.0f;
-            const float chain =
-                __fmul_rn(__fdiv_rn(__fmul_rn(cov, __fsub_rn(1.0f, cov)), sig), sign);
-            const float ka = __fmul_rn(chain, -__fsub_rn(1.0f, t));
-            const float kb = __fmul_rn(chain, -t);
-            float cax = __fmul_rn(ka, ux), cay = __fmul_rn(ka, uy);
-            float cbx = __fmul_rn(kb, ux), cby = __fmul_rn(kb, uy);
-#pragma unroll
-            for (int q = 0; q < 3; ++q) {
-              coef[2 * q] = (q == ea) ? cax : ((q == eb) ? cbx : 0.0f);
-              coef[2 * q + 1] = (q == ea) ? cay : ((q == eb) ? cby : 0.0f);
-            }
-          }
-#pragma unroll
-          for (int q = 0; q < 6; ++q) gv[q] = __fmul_rn(d_cov, coef[q]);
-          // composite (raster.rs:63)
-          r0 = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(r0, om));
-          r1 = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(r1, om));
-          r2 = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(r2, om));
+        if (!active[q] || !eval_pair<true, kStrict>(r, code, px, py[q], ptx, pty[q], K, pe))
+          continue;
+        contrib = true;
+        const float w = pe.w, om = __fsub_rn(1.0f, w);
+        Q[q].mul(om, k);
+        const float A = attenuation<kStrict>(P[q], Q[q], k);
+        const float g0 = __fmul_rn(G0[q], A), g1 = __fmul_rn(G1[q], A), g2 = __fmul_rn(G2[q], A);
+        // grad.rs:162-179
+        acc[6] = __fmaf_rn(g0, w, acc[6]);
+        acc[7] = __fmaf_rn(g1, w, acc[7]);
+        acc[8] = __fmaf_rn(g2, w, acc[8]);
+        float d_w = __fmul_rn(g0, __fsub_rn(r.color[0], r0[q]));
+        d_w = __fmaf_rn(g1, __fsub_rn(r.color[1], r1[q]), d_w);
+        d_w = __fmaf_rn(g2, __fsub_rn(r.color[2], r2[q]), d_w);
+        if (r.flags & kAlphaActive) acc[9] = __fmaf_rn(d_w, pe.cov, acc[9]);
+        // coverage_with_grad (grad.rs:231-270): nonzero only in the band and
+        // away from the boundary itself (dist >= 1e-9).
+        if (pe.band && !(pe.dist < 1e-9f)) {
+          band = true;
+          const float d_cov = __fmul_rn(d_w, r.alpha);
+          const float cov = pe.cov, t = pe.t;
+          const float chain = __fmul_rn(__fmul_rn(cov, __fsub_rn(1.0f, cov)),
+                                        pe.inside ? K.inv_sigma : -K.inv_sigma);
+          const float kA = __fmul_rn(d_cov, __fmul_rn(chain, __fsub_rn(t, 1.0f)));
+          const float kB = __fmul_rn(d_cov, __fmul_rn(chain, -t));
+          const float ax = __fmul_rn(kA, pe.ux), ay = __fmul_rn(kA, pe.uy);
+          const float bx = __fmul_rn(kB, pe.ux), by = __fmul_rn(kB, pe.uy);
+          const int e = pe.edge;
+          acc[0] += (e == 0) ? ax : ((e == 2) ? bx : 0.0f);
+          acc[1] += (e == 0) ? ay : ((e == 2) ? by : 0.0f);
+          acc[2] += (e == 1) ? ax : ((e == 0) ? bx : 0.0f);
+          acc[3] += (e == 1) ? ay : ((e == 0) ? by : 0.0f);
+          acc[4] += (e == 2) ? ax : ((e == 1) ? bx : 0.0f);
+          acc[5] += (e == 2) ? ay : ((e == 1) ? by : 0.0f);
         }
+        r0[q] = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(r0[q], om));  // raster.rs:63
+        r1[q] = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(r1[q], om));
+        r2[q] = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(r2[q], om));
       }
-      // Block reduction: warp shuffles, then one shared atomic per warp.
-      if (__any_sync(0xffffffffu, contrib)) {
-        float s6 = warp_sum(gc0), s7 = warp_sum(gc1), s8 = warp_sum(gc2), s9 = warp_sum(ga);
-        if (lane == 0) {
-          atomicAdd(&sm.acc[j][6], s6);
-          atomicAdd(&sm.acc[j][7], s7);
-          atomicAdd(&sm.acc[j][8], s8);
-          atomicAdd(&sm.acc[j][9], s9);
-        }
-        if (!(ef & kTileInside)) {
-#pragma unroll
-          for (int q = 0; q < 6; ++q) {
-            float s = warp_sum(gv[q]);
-            if (lane == 0) atomicAdd(&sm.acc[j][q], s);
-          }
-        }
+      // Per warp: one transposed reduction, then one shared atomic per value.
+      const unsigned any = __ballot_sync(0xffffffffu, contrib);
+      if (any == 0u) continue;
+      if (__any_sync(0xffffffffu, band)) {
+        const float s = reduce10(acc, lane);
+        if (slot10 >= 0) atomicAdd(&sm.acc[j][slot10], s);
+      } else {
+        const float s = reduce4(acc[6], acc[7], acc[8], acc[9], lane);
+        if ((lane & 7) == 0) atomicAdd(&sm.acc[j][6 + (lane >> 3)], s);
       }
     }
     __syncthreads();
     // One global atomic per (triangle, parameter) per block.
     float* g = a.grads + (size_t)b * a.T * kParams;
     for (int i = threadIdx.x; i < count * kParams; i += kThreads) {
-      float v = (&sm.acc[0][0])[i];
+      const float v = (&sm.acc[0][0])[i];
       if (v != 0.0f) atomicAdd(&g[(size_t)sm.kidx[i / kParams] * kParams + (i % kParams)], v);
     }
   }
@@ -524,7 +723,7 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
       for (int w = 0; w < kWarps; ++w) s += sm.loss_part[w];
       a.loss_partials[(size_t)b * n_tiles + local_tile] = s;
       __threadfence();
-      unsigned prev = atomicAdd(&a.loss_counters[b], 1u);
+      const unsigned prev = atomicAdd(&a.loss_counters[b], 1u);
       sm.is_last = (prev == (unsigned)(n_tiles - 1));
     }
     __syncthreads();
@@ -677,19 +876,27 @@ cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
 
 static_assert(sizeof(Smem) <= 48 * 1024, "raster smem must fit the default 48 KB limit");
 
-template <int Mode> static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
-  const size_t smem = sizeof(Smem);
+template <int Mode, bool kStrict>
+static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
   dim3 grid(n_tiles, a.B);
-  dr_raster_kernel<Mode><<<grid, kThreads, smem, s>>>(a);
+  dr_raster_kernel<Mode, kStrict><<<grid, kThreads, sizeof(Smem), s>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s) {
   if (a.B == 0 || n_tiles == 0) return cudaSuccess;
-  switch (mode) {
-    case kModeRender: return launch_mode<kModeRender>(a, n_tiles, s);
-    case kModeLoss: return launch_mode<kModeLoss>(a, n_tiles, s);
-    case kModeGrad: return launch_mode<kModeGrad>(a, n_tiles, s);
+  if (a.strict) {
+    switch (mode) {
+      case kModeRender: return launch_mode<kModeRender, true>(a, n_tiles, s);
+      case kModeLoss: return launch_mode<kModeLoss, true>(a, n_tiles, s);
+      case kModeGrad: return launch_mode<kModeGrad, true>(a, n_tiles, s);
+    }
+  } else {
+    switch (mode) {
+      case kModeRender: return launch_mode<kModeRender, false>(a, n_tiles, s);
+      case kModeLoss: return launch_mode<kModeLoss, false>(a, n_tiles, s);
+      case kModeGrad: return launch_mode<kModeGrad, false>(a, n_tiles, s);
+    }
   }
   return cudaErrorInvalidValue;
 }

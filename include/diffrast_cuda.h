@@ -91,6 +91,13 @@ DR_API int dr_device_count(void);
 /* Where `background` pointers live: 0 = host memory (default), 1 = device. */
 DR_API dr_status dr_set_background_location(dr_ctx* ctx, int on_device);
 
+/* Strict parity mode (off by default). On: every soft-edge pixel evaluates the
+ * reference's f32 expressions operation for operation (IEEE division and
+ * sqrt, no contraction: raster.rs:96-134, grad.rs:231-270) instead of the fast
+ * MUFU forms, at several times the cost. No reference counterpart (the
+ * reference has a single precision mode); for bisecting parity questions. */
+DR_API dr_status dr_set_strict(dr_ctx* ctx, int strict);
+
 /* --- hot path ------------------------------------------------------------ */
 
 /* Forward render of a batch into `image` (layout as given).

@@ -280,3 +280,36 @@ def test_adam_is_bit_exact(native, oracle):
         oracle.project(p_ref)
         native.adam_step(P, M, V, cuda(g), step)
         assert np.array_equal(host(P), p_ref, equal_nan=True), step
+
+
+@pytest.fixture()
+def strict(native):
+    native.set_strict(True)
+    yield
+    native.set_strict(False)
+
+
+@pytest.mark.parametrize("W,H,T", [(37, 19, 33), (64, 64, 32), (96, 80, 200)])
+def test_strict_mode_matches_oracle(native, oracle, strict, W, H, T):
+    from diffrast.scenes import uniform_scenes
+
+    params = uniform_scenes(2, T, seed=W + H + T)
+    target = oracle.render_batch(uniform_scenes(2, T, seed=99), H, W, 0.01)
+    run_all(native, oracle, params, target, 0.01)
+
+
+def test_strict_and_fast_modes_agree(native, oracle):
+    from diffrast.scenes import config2_params
+
+    p, tp = config2_params(4, 128, 5)
+    P = cuda(p)
+    tgt = native.render(cuda(tp), 128, 128, 0.0015)
+    lf, gf, imf = native.loss_backward(P, tgt, 0.0015, want_image=True)
+    native.set_strict(True)
+    try:
+        ls, gs, ims = native.loss_backward(P, tgt, 0.0015, want_image=True)
+    finally:
+        native.set_strict(False)
+    assert_images_close(host(imf), host(ims), "fast vs strict render")
+    np.testing.assert_allclose(host(lf), host(ls), rtol=1e-5)
+    assert_grads_close(host(gf), host(gs), "fast vs strict grads")
