@@ -85,7 +85,7 @@ struct dr_ctx {
   int device = 0;
   std::mutex mu;
   int bg_on_device = 0;
-  int strict = 0;
+  int precision = 0;
   uint64_t hits = 0, misses = 0;
   Slot recs, partials, counters, bgbuf;
   // fit state
@@ -183,7 +183,7 @@ dr_status prepare(dr_ctx* ctx, const float* params, const float* background, int
   a.tile_row_step = 1;
   a.sigma_eff = std::fmax(sigma, 1e-8f);  // raster.rs:75 sigma.max(1e-8)
   a.inv_sigma = (float)(1.0 / (double)a.sigma_eff);
-  a.strict = ctx->strict;
+  a.precision = ctx->precision;
   a.rej = kRejectSigmas * a.sigma_eff;
   a.acc = kAcceptSigmas * a.sigma_eff;
   a.layout = layout;
@@ -344,10 +344,12 @@ dr_status dr_set_background_location(dr_ctx* ctx, int on_device) {
   return DR_OK;
 }
 
-dr_status dr_set_strict(dr_ctx* ctx, int strict) {
+dr_status dr_set_precision(dr_ctx* ctx, int precision) {
   if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (precision < DR_PRECISION_REFERENCE || precision > DR_PRECISION_FAST)
+    return fail(DR_INVALID_ARGUMENT, "unknown precision mode %d", precision);
   std::lock_guard<std::mutex> lock(ctx->mu);
-  ctx->strict = strict ? 1 : 0;
+  ctx->precision = precision;
   if (ctx->fit_exec) {
     cudaGraphExecDestroy(ctx->fit_exec);
     ctx->fit_exec = nullptr;
@@ -612,7 +614,7 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       a.tile_row_step = 1;
       a.sigma_eff = std::fmax(sigma, 1e-8f);
       a.inv_sigma = (float)(1.0 / (double)a.sigma_eff);
-      a.strict = ctx->strict;
+      a.precision = ctx->precision;
       a.rej = kRejectSigmas * a.sigma_eff;
       a.acc = kAcceptSigmas * a.sigma_eff;
       a.bg3[0] = bg[0];

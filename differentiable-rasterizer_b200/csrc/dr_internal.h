@@ -20,7 +20,7 @@ struct RasterArgs {
   int tile_row0, tile_row_step;  // tile rows covered: row0 + i * step
   float sigma_eff;               // max(sigma, 1e-8) (raster.rs:75)
   float inv_sigma;               // 1 / sigma_eff
-  int strict;                    // 1: band pairs use the reference's exact arithmetic
+  int precision;                 // 0 reference rounding, 1 strict, 2 fast (band arithmetic)
   float rej, acc;                // fast-path thresholds (normalized units)
   float bg3[3];                  // shared background when bg_dev is null
   const float* bg_dev;           // device background: 3 floats, or B*3 when bg_per_scene

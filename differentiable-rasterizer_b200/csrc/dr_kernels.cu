@@ -28,11 +28,16 @@
 
 namespace dr {
 
+#ifndef DR_PPT
+#define DR_PPT 1
+#endif
 constexpr int kTile = 16;
-constexpr int kPPT = 2;                                  // pixels per thread
-constexpr int kWarps = 4;                                // 8x8 warp blocks per tile
+constexpr int kPPT = DR_PPT;                             // pixels per thread (1 or 2)
+constexpr int kBlockW = 8, kBlockH = 4 * kPPT;           // one warp's pixel block
+constexpr int kWarps = (kTile / kBlockW) * (kTile / kBlockH);
 constexpr int kThreads = kWarps * 32;
-constexpr int kChunk = kThreads;                         // triangles binned per round
+static_assert(kWarps <= 8, "block codes pack 4 bits per warp into one int");
+constexpr int kChunk = 128;                              // triangles binned per round (<= kThreads)
 constexpr float kRenorm = 18446744073709551616.0f;        // 2^64
 constexpr float kRenormInv = 5.42101086242752217e-20f;    // 2^-64
 
@@ -172,8 +177,6 @@ __global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W,
 // so whole warps skip or take the cheap path on a uniform branch.
 
 constexpr int kBlkSkip = 1, kBlkBox = 2, kBlkInside = 4;
-constexpr int kBlockW = 8, kBlockH = 4 * kPPT;
-
 struct Smem {
   TriRec rec[kChunk];
   int bcode[kChunk];
@@ -261,97 +264,193 @@ struct Consts {
   float sigma_eff, inv_sigma, rej, acc;
 };
 
-// What one (pixel, triangle) pair contributes. `band` means the coverage
-// came from the full geometry (else cov == 1 exactly). The gradient fields
-// are filled only when kGrad.
+// Precision modes of the soft-edge (band) arithmetic.
+//   kPrecRef     default: cheap classification and nearest-edge choice, then
+//                the nearest edge's distance, the sigmoid, and the gradient
+//                direction with the reference's f32 operations and rounding
+//                (raster.rs:124-134, grad.rs:231-270). Near an edge those f32
+//                values carry cancellation error of ~1e-7 / dist, which the
+//                reference's outputs contain and which this mode reproduces.
+//   kPrecStrict  every edge with the reference's exact arithmetic.
+//   kPrecFast    exact-math shortcuts (distance = nearest edge line inside,
+//                gradient direction = the edge normal) with MUFU reciprocals:
+//                closer to the true (f64) gradient, not to the f32 reference.
+enum Prec : int { kPrecRef = 0, kPrecStrict = 1, kPrecFast = 2 };
+
+// What one (pixel, triangle) pair contributes. `band` is false when the
+// vertex gradient is exactly zero (cov == 1, or dist < 1e-9 as
+// grad.rs:252-254). With kGrad, a band pair also carries d(cov)/d(vertex) for
+// the two vertices of its nearest edge: (dax, day) for vertex `edge`,
+// (dbx, dby) for vertex `edge + 1` (grad.rs:264-268).
 struct PairEval {
   float w, cov;
-  bool band, inside;
-  float dist, t, ux, uy;
+  bool band;
+  float dax, day, dbx, dby;
   int edge;
 };
 
-// raster.rs:96-106 sigmoid of the signed distance, fast form: one ex2 and one
-// rcp on the MUFU pipe. Same branch structure as raster.rs:79-87.
+// Reciprocal and square root rounded to nearest without the library's
+// special-case branches: the hardware approximation (rcp.approx / rsqrt.approx,
+// relative error below 2^-22) refined by one Newton-Raphson step with an FMA
+// residual (Markstein's method). The refined value is within ~2^-44 of the
+// exact result, so it rounds correctly except for inputs whose exact result
+// lies that close to a rounding midpoint. Valid for normal, positive inputs.
+__device__ __forceinline__ float rcp_approx(float y) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
+  return r;
+}
+__device__ __forceinline__ float rsqrt_approx(float x) {
+  float r;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float rcp_nr(float y) {
+  const float r = rcp_approx(y);
+  return __fmaf_rn(r, __fmaf_rn(-y, r, 1.0f), r);
+}
+// sqrt(x) for x >= 0; inputs below 1e-30 (distances far under the 1e-9 cut
+// of grad.rs:252) return 0.
+__device__ __forceinline__ float sqrt_nr(float x) {
+  const float rs = rsqrt_approx(x);
+  const float s = __fmul_rn(x, rs);
+  const float res = __fmaf_rn(-s, s, x);
+  const float out = __fmaf_rn(res, __fmul_rn(0.5f, rs), s);
+  return x > 1e-30f ? out : 0.0f;
+}
+
+// a / b rounded to nearest, given inv_b = RN(1 / b): one correction step on
+// the product (an FMA residual), which yields the correctly rounded quotient
+// except in rare boundary cases.
+__device__ __forceinline__ float div_rn_inv(float a, float b, float inv_b) {
+  const float q0 = __fmul_rn(a, inv_b);
+  const float r = __fmaf_rn(-q0, b, a);
+  return __fmaf_rn(r, inv_b, q0);
+}
+
+// Sigmoid of raster.rs:79-87 with its rounding: RN(1 / RN(1 + e)) for x >= 0,
+// RN(e / RN(1 + e)) below, e = exp(-|x|). The exponential may be approximate:
+// its error moves 1 + e by far less than an ulp of 1 wherever e is small,
+// while near cov == 1 the gradient uses 1 - cov, which depends on exactly how
+// the reference rounded cov.
+__device__ __forceinline__ float sigmoid_rounded(float x) {
+  const float e = __expf(-fabsf(x));
+  const float y = __fadd_rn(1.0f, e);
+  const float ry = rcp_nr(y);
+  return x >= 0.0f ? ry : div_rn_inv(e, y, ry);
+}
+
 __device__ __forceinline__ float sigmoid_fast(float x) {
   const float e = __expf(-fabsf(x));
-  const float r = __fdividef(1.0f, __fadd_rn(1.0f, e));
-  return x >= 0.0f ? r : __fmul_rn(e, r);
+  return __fdividef(x >= 0.0f ? 1.0f : e, __fadd_rn(1.0f, e));
+}
+
+// d(cov)/d(vertices) for the nearest edge with the reference's rounding:
+// cp = a + t (b - a); u = (pt - cp) / dist; chain = cov (1 - cov) / sigma * sign;
+// d[a] = chain * -(1 - t) * u, d[b] = chain * -t * u (grad.rs:256-268).
+__device__ __forceinline__ void cov_grad_ref(const TriRec& r, int edge, float t, float dist,
+                                             float cov, bool inside, float ptx, float pty,
+                                             const Consts& K, PairEval& o) {
+  const float ax = r.v[2 * edge], ay = r.v[2 * edge + 1];
+  const float cpx = __fadd_rn(ax, __fmul_rn(t, r.e[2 * edge]));
+  const float cpy = __fadd_rn(ay, __fmul_rn(t, r.e[2 * edge + 1]));
+  const float rd = rcp_nr(dist);
+  const float ux = div_rn_inv(__fsub_rn(ptx, cpx), dist, rd);
+  const float uy = div_rn_inv(__fsub_rn(pty, cpy), dist, rd);
+  float chain = div_rn_inv(__fmul_rn(cov, __fsub_rn(1.0f, cov)), K.sigma_eff, K.inv_sigma);
+  chain = inside ? chain : -chain;
+  const float ka = __fmul_rn(chain, -__fsub_rn(1.0f, t));
+  const float kb = __fmul_rn(chain, -t);
+  o.dax = __fmul_rn(ka, ux);
+  o.day = __fmul_rn(ka, uy);
+  o.dbx = __fmul_rn(kb, ux);
+  o.dby = __fmul_rn(kb, uy);
+  o.edge = edge;
 }
 
 // Exact reference arithmetic for one pair (degenerate triangles, NaN alpha,
-// and every band pair in strict mode): raster.rs:96-106 + grad.rs:231-270.
+// near-tie pixels, and every band pair in strict mode): raster.rs:96-106 +
+// grad.rs:231-270. Kept out of line: it is rare on the default path, and
+// inlining its IEEE divisions at every call site overflows the instruction
+// cache of the hot loop.
 template <bool kGrad>
-__device__ __forceinline__ bool eval_ref(const TriRec& r, float ptx, float pty, const Consts& K,
-                                         PairEval& o) {
+__device__ __noinline__ bool eval_ref(const TriRec& r, float ptx, float pty, const Consts& K,
+                                      PairEval& o) {
   const SdResult g = signed_distance_ref(r.v, r.e, r.len2, ptx, pty);
   o.cov = sigmoid_ref(__fdiv_rn(g.sd, K.sigma_eff));
   o.w = __fmul_rn(r.alpha, o.cov);
-  o.band = true;
-  o.inside = g.sd > 0.0f;
-  if (kGrad) {
-    o.dist = g.dist;
-    o.t = g.t;
-    o.edge = g.edge;
+  o.band = !(g.dist < 1e-9f);
+  if (kGrad && o.band) {
     const float ax = r.v[2 * g.edge], ay = r.v[2 * g.edge + 1];
     const float cpx = __fadd_rn(ax, __fmul_rn(g.t, r.e[2 * g.edge]));
     const float cpy = __fadd_rn(ay, __fmul_rn(g.t, r.e[2 * g.edge + 1]));
-    o.ux = __fdiv_rn(__fsub_rn(ptx, cpx), g.dist);
-    o.uy = __fdiv_rn(__fsub_rn(pty, cpy), g.dist);
+    const float ux = __fdiv_rn(__fsub_rn(ptx, cpx), g.dist);
+    const float uy = __fdiv_rn(__fsub_rn(pty, cpy), g.dist);
+    float chain = __fdiv_rn(__fmul_rn(o.cov, __fsub_rn(1.0f, o.cov)), K.sigma_eff);
+    chain = (g.sd > 0.0f) ? chain : -chain;
+    const float ka = __fmul_rn(chain, -__fsub_rn(1.0f, g.t));
+    const float kb = __fmul_rn(chain, -g.t);
+    o.dax = __fmul_rn(ka, ux);
+    o.day = __fmul_rn(ka, uy);
+    o.dbx = __fmul_rn(kb, ux);
+    o.dby = __fmul_rn(kb, uy);
+    o.edge = g.edge;
   }
   return !(o.w <= kMinWeight);
 }
 
-// One pair, given the warp block's code. Returns true when the pair
-// composites (w > MIN_WEIGHT). The arithmetic that decides w uses explicit
-// rounding intrinsics only, so the forward pass and the gradient pass (two
+// One pair, given the warp block's code. Returns kSkip (no contribution),
+// kHit (composites: w > MIN_WEIGHT, `o` filled) or kExact (the caller must
+// evaluate it with eval_ref). The arithmetic that decides w uses explicit
+// rounding only, so the forward pass and the gradient pass (two
 // instantiations) compute bit-identical w.
-template <bool kGrad, bool kStrict>
-__device__ __forceinline__ bool eval_pair(const TriRec& r, int code, int px, int py, float ptx,
+enum PairStatus : int { kSkip = 0, kHit = 1, kExact = 2 };
+
+template <bool kGrad, int kPrec>
+__device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int py, float ptx,
                                           float pty, const Consts& K, PairEval& o) {
   if (code & kBlkBox) {
-    if (px < r.bbox[0] || px >= r.bbox[2] || py < r.bbox[1] || py >= r.bbox[3]) return false;
+    if (px < r.bbox[0] || px >= r.bbox[2] || py < r.bbox[1] || py >= r.bbox[3]) return kSkip;
   }
   if (code & kBlkInside) {
     o.cov = 1.0f;
     o.w = r.alpha;
     o.band = false;
-    return true;  // alpha > MIN_WEIGHT is guaranteed by the set-up cull
+    return kHit;  // alpha > MIN_WEIGHT is guaranteed by the set-up cull
   }
-  if (!(r.flags & kFastOk)) return eval_ref<kGrad>(r, ptx, pty, K, o);
+  if (!(r.flags & kFastOk)) return kExact;
   const float l0 = __fmaf_rn(r.n[0], ptx, __fmaf_rn(r.n[1], pty, r.c[0]));
   const float l1 = __fmaf_rn(r.n[2], ptx, __fmaf_rn(r.n[3], pty, r.c[1]));
   const float l2 = __fmaf_rn(r.n[4], ptx, __fmaf_rn(r.n[5], pty, r.c[2]));
   const float mn = fminf(fminf(l0, l1), l2);
-  if (mn < -(K.rej + r.margin)) return false;
+  if (mn < -(K.rej + r.margin)) return kSkip;
   if (mn > K.acc + r.margin) {
     o.cov = 1.0f;
     o.w = r.alpha;
     o.band = false;
-    return true;
+    return kHit;
   }
-  if (kStrict) return eval_ref<kGrad>(r, ptx, pty, K, o);
-  // Inside a convex polygon the nearest boundary point is the foot on the
-  // nearest edge line, so the distance is min_i l_i and the direction from it
-  // is that edge's inward normal. Outside, the distance is the smallest
-  // clamped segment distance (raster.rs:124-134).
+  if (kPrec == kPrecStrict) return kExact;
+
+  // Within rounding distance of an edge line the inside/outside call, and
+  // inside near an angle bisector the choice of nearest edge, could differ
+  // from the reference's f32 decision; those rare pixels take the exact path.
+  if (fabsf(mn) < r.margin) return kExact;
+
+  // Nearest edge. Inside a convex polygon the nearest boundary point is the
+  // foot on the nearest edge line (min_i l_i); outside it is the smallest
+  // clamped segment distance (raster.rs:124-134), a unique point.
   const bool inside = mn >= 0.0f;
-  float dist, t = 0.0f, ux = 0.0f, uy = 0.0f;
   int edge = 0;
+  float fdist = mn, ft = 0.0f, fdx = 0.0f, fdy = 0.0f, frs = 0.0f;
   if (inside) {
-    dist = mn;
-    if (kGrad) {
-      float best = l0;
-      if (l1 < best) { best = l1; edge = 1; }
-      if (l2 < best) { edge = 2; }
-      const float ex = r.e[2 * edge], ey = r.e[2 * edge + 1];
-      const float apx = __fsub_rn(ptx, r.v[2 * edge]), apy = __fsub_rn(pty, r.v[2 * edge + 1]);
-      t = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[edge]));
-      ux = r.n[2 * edge];
-      uy = r.n[2 * edge + 1];
-    }
+    float best = l0, second = __int_as_float(0x7f800000);
+    if (l1 < best) { second = best; best = l1; edge = 1; } else { second = l1; }
+    if (l2 < best) { second = best; edge = 2; } else { second = fminf(second, l2); }
+    if (second - best < r.margin) return kExact;
   } else {
-    float bd2 = __int_as_float(0x7f800000), bdx = 0.0f, bdy = 0.0f;
+    float bd2 = __int_as_float(0x7f800000), sd2 = bd2, st = 0.0f;
+    int sedge = 0;
 #pragma unroll
     for (int e = 0; e < 3; ++e) {
       const float ex = r.e[2 * e], ey = r.e[2 * e + 1];
@@ -360,33 +459,83 @@ __device__ __forceinline__ bool eval_pair(const TriRec& r, int code, int px, int
       const float dx = __fmaf_rn(-te, ex, apx), dy = __fmaf_rn(-te, ey, apy);
       const float d2 = __fmaf_rn(dx, dx, __fmul_rn(dy, dy));
       if (d2 < bd2) {
+        sd2 = bd2;
+        st = ft;
+        sedge = edge;
         bd2 = d2;
-        bdx = dx;
-        bdy = dy;
-        t = te;
+        fdx = dx;
+        fdy = dy;
+        ft = te;
         edge = e;
+      } else if (d2 < sd2) {
+        sd2 = d2;
+        st = te;
+        sedge = e;
       }
     }
-    const float rs = rsqrtf(bd2);
-    dist = bd2 > 0.0f ? __fmul_rn(bd2, rs) : 0.0f;
-    if (kGrad) {
-      ux = __fmul_rn(bdx, rs);
-      uy = __fmul_rn(bdy, rs);
+    frs = rsqrtf(bd2);
+    fdist = bd2 > 0.0f ? __fmul_rn(bd2, frs) : 0.0f;
+    // Two edges within rounding distance of each other (a sliver, or two
+    // nearly parallel edges) could be ordered differently by the reference's
+    // f32 distances, sending this pixel's gradient to another vertex pair:
+    // take the exact path. Adjacent edges both clamped to their shared
+    // vertex describe the same point and are not a real tie.
+    const bool same_vertex = (sedge == (edge + 1) % 3) ? (ft == 1.0f && st == 0.0f)
+                                                       : (ft == 0.0f && st == 1.0f);
+    if (!same_vertex &&
+        sd2 - bd2 < __fmul_rn(r.margin, __fmaf_rn(2.0f, fdist, r.margin)))
+      return kExact;
+  }
+
+  if (kPrec == kPrecFast) {
+    const float x = __fmul_rn(inside ? fdist : -fdist, K.inv_sigma);
+    o.cov = sigmoid_fast(x);
+    o.w = __fmul_rn(r.alpha, o.cov);
+    o.band = !(fdist < 1e-9f);
+    if (kGrad && o.band) {
+      float t = ft, ux, uy;
+      if (inside) {
+        const float ex = r.e[2 * edge], ey = r.e[2 * edge + 1];
+        const float apx = __fsub_rn(ptx, r.v[2 * edge]), apy = __fsub_rn(pty, r.v[2 * edge + 1]);
+        t = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[edge]));
+        ux = r.n[2 * edge];
+        uy = r.n[2 * edge + 1];
+      } else {
+        ux = __fmul_rn(fdx, frs);
+        uy = __fmul_rn(fdy, frs);
+      }
+      const float cov = o.cov;
+      const float chain = __fmul_rn(__fmul_rn(cov, __fsub_rn(1.0f, cov)),
+                                    inside ? K.inv_sigma : -K.inv_sigma);
+      const float ka = __fmul_rn(chain, __fsub_rn(t, 1.0f)), kb = __fmul_rn(chain, -t);
+      o.dax = __fmul_rn(ka, ux);
+      o.day = __fmul_rn(ka, uy);
+      o.dbx = __fmul_rn(kb, ux);
+      o.dby = __fmul_rn(kb, uy);
+      o.edge = edge;
     }
+    return o.w <= kMinWeight ? kSkip : kHit;
   }
-  const float x = __fmul_rn(inside ? dist : -dist, K.inv_sigma);
-  o.cov = sigmoid_fast(x);
+
+  // kPrecRef: the nearest edge's segment distance exactly as
+  // point_segment_distance computes it (raster.rs:124-134).
+  const float ax = r.v[2 * edge], ay = r.v[2 * edge + 1];
+  const float ex = r.e[2 * edge], ey = r.e[2 * edge + 1], len2 = r.len2[edge];
+  const float apx = __fsub_rn(ptx, ax), apy = __fsub_rn(pty, ay);
+  float t = 0.0f;
+  if (!(len2 <= 1e-20f)) {
+    const float dot = __fadd_rn(__fmul_rn(apx, ex), __fmul_rn(apy, ey));
+    t = rclamp(div_rn_inv(dot, len2, r.il[edge]), 0.0f, 1.0f);
+  }
+  const float dx = __fsub_rn(apx, __fmul_rn(t, ex));
+  const float dy = __fsub_rn(apy, __fmul_rn(t, ey));
+  const float dist = sqrt_nr(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)));
+  const float sd = inside ? dist : -dist;
+  o.cov = sigmoid_rounded(div_rn_inv(sd, K.sigma_eff, K.inv_sigma));
   o.w = __fmul_rn(r.alpha, o.cov);
-  o.band = true;
-  o.inside = inside && dist > 0.0f;
-  if (kGrad) {
-    o.dist = dist;
-    o.t = t;
-    o.edge = edge;
-    o.ux = ux;
-    o.uy = uy;
-  }
-  return !(o.w <= kMinWeight);
+  o.band = !(dist < 1e-9f);
+  if (kGrad && o.band) cov_grad_ref(r, edge, t, dist, o.cov, sd > 0.0f, ptx, pty, K, o);
+  return o.w <= kMinWeight ? kSkip : kHit;
 }
 
 // Running product of (1 - w) with 2^64 renormalisation and barrier tracking.
@@ -423,11 +572,12 @@ struct Prod {
 // A_k = prod over layers above k of (1 - w), from the full product P (after
 // the last layer) and the running product Q (through layer k). A barrier
 // layer resets Q to 1, so the same ratio yields the product above it.
-template <bool kStrict>
+template <int kPrec>
 __device__ __forceinline__ float attenuation(const Prod& P, const Prod& Q, int k) {
   if (k < P.zn) return __int_as_float(0x7fc00000);
   if (k < P.z0) return 0.0f;
-  const float ratio = kStrict ? __fdiv_rn(P.m, Q.m) : __fdividef(P.m, Q.m);
+  const float ratio =
+      kPrec == kPrecFast ? __fdividef(P.m, Q.m) : div_rn_inv(P.m, Q.m, rcp_nr(Q.m));
   const int de = P.e - Q.e;
   if (de == 0) return ratio;
   if (de == 1) return __fmul_rn(ratio, kRenormInv);
@@ -514,7 +664,7 @@ __device__ __forceinline__ size_t pix_index(int layout, int b, int ch, int px, i
   return (((size_t)b * H + py) * W + px) * 3 + ch;
 }
 
-template <int Mode, bool kStrict>
+template <int Mode, int kPrec>
 __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -575,9 +725,11 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
       const int k = sm.kidx[j];
 #pragma unroll
       for (int q = 0; q < kPPT; ++q) {
+        if (!active[q]) continue;
         PairEval pe;
-        if (!active[q] || !eval_pair<false, kStrict>(r, code, px, py[q], ptx, pty[q], K, pe))
-          continue;
+        int st = eval_pair<false, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
+        if (st == kExact) st = eval_ref<false>(r, ptx, pty[q], K, pe) ? kHit : kSkip;
+        if (st == kSkip) continue;
         const float w = pe.w, om = __fsub_rn(1.0f, w);
         c0[q] = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(c0[q], om));  // raster.rs:63
         c1[q] = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(c1[q], om));
@@ -654,13 +806,15 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
       bool contrib = false, band = false;
 #pragma unroll
       for (int q = 0; q < kPPT; ++q) {
+        if (!active[q]) continue;
         PairEval pe;
-        if (!active[q] || !eval_pair<true, kStrict>(r, code, px, py[q], ptx, pty[q], K, pe))
-          continue;
+        int st = eval_pair<true, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
+        if (st == kExact) st = eval_ref<true>(r, ptx, pty[q], K, pe) ? kHit : kSkip;
+        if (st == kSkip) continue;
         contrib = true;
         const float w = pe.w, om = __fsub_rn(1.0f, w);
         Q[q].mul(om, k);
-        const float A = attenuation<kStrict>(P[q], Q[q], k);
+        const float A = attenuation<kPrec>(P[q], Q[q], k);
         const float g0 = __fmul_rn(G0[q], A), g1 = __fmul_rn(G1[q], A), g2 = __fmul_rn(G2[q], A);
         // grad.rs:162-179
         acc[6] = __fmaf_rn(g0, w, acc[6]);
@@ -670,18 +824,13 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
         d_w = __fmaf_rn(g1, __fsub_rn(r.color[1], r1[q]), d_w);
         d_w = __fmaf_rn(g2, __fsub_rn(r.color[2], r2[q]), d_w);
         if (r.flags & kAlphaActive) acc[9] = __fmaf_rn(d_w, pe.cov, acc[9]);
-        // coverage_with_grad (grad.rs:231-270): nonzero only in the band and
+        // coverage_with_grad (grad.rs:231-270): nonzero only for band pairs
         // away from the boundary itself (dist >= 1e-9).
-        if (pe.band && !(pe.dist < 1e-9f)) {
+        if (pe.band) {
           band = true;
           const float d_cov = __fmul_rn(d_w, r.alpha);
-          const float cov = pe.cov, t = pe.t;
-          const float chain = __fmul_rn(__fmul_rn(cov, __fsub_rn(1.0f, cov)),
-                                        pe.inside ? K.inv_sigma : -K.inv_sigma);
-          const float kA = __fmul_rn(d_cov, __fmul_rn(chain, __fsub_rn(t, 1.0f)));
-          const float kB = __fmul_rn(d_cov, __fmul_rn(chain, -t));
-          const float ax = __fmul_rn(kA, pe.ux), ay = __fmul_rn(kA, pe.uy);
-          const float bx = __fmul_rn(kB, pe.ux), by = __fmul_rn(kB, pe.uy);
+          const float ax = __fmul_rn(d_cov, pe.dax), ay = __fmul_rn(d_cov, pe.day);
+          const float bx = __fmul_rn(d_cov, pe.dbx), by = __fmul_rn(d_cov, pe.dby);
           const int e = pe.edge;
           acc[0] += (e == 0) ? ax : ((e == 2) ? bx : 0.0f);
           acc[1] += (e == 0) ? ay : ((e == 2) ? by : 0.0f);
@@ -876,27 +1025,29 @@ cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
 
 static_assert(sizeof(Smem) <= 48 * 1024, "raster smem must fit the default 48 KB limit");
 
-template <int Mode, bool kStrict>
+template <int Mode, int kPrec>
 static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
   dim3 grid(n_tiles, a.B);
-  dr_raster_kernel<Mode, kStrict><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  dr_raster_kernel<Mode, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
   return cudaGetLastError();
+}
+
+template <int kPrec>
+static cudaError_t launch_prec(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s) {
+  switch (mode) {
+    case kModeRender: return launch_mode<kModeRender, kPrec>(a, n_tiles, s);
+    case kModeLoss: return launch_mode<kModeLoss, kPrec>(a, n_tiles, s);
+    case kModeGrad: return launch_mode<kModeGrad, kPrec>(a, n_tiles, s);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s) {
   if (a.B == 0 || n_tiles == 0) return cudaSuccess;
-  if (a.strict) {
-    switch (mode) {
-      case kModeRender: return launch_mode<kModeRender, true>(a, n_tiles, s);
-      case kModeLoss: return launch_mode<kModeLoss, true>(a, n_tiles, s);
-      case kModeGrad: return launch_mode<kModeGrad, true>(a, n_tiles, s);
-    }
-  } else {
-    switch (mode) {
-      case kModeRender: return launch_mode<kModeRender, false>(a, n_tiles, s);
-      case kModeLoss: return launch_mode<kModeLoss, false>(a, n_tiles, s);
-      case kModeGrad: return launch_mode<kModeGrad, false>(a, n_tiles, s);
-    }
+  switch (a.precision) {
+    case kPrecRef: return launch_prec<kPrecRef>(mode, a, n_tiles, s);
+    case kPrecStrict: return launch_prec<kPrecStrict>(mode, a, n_tiles, s);
+    case kPrecFast: return launch_prec<kPrecFast>(mode, a, n_tiles, s);
   }
   return cudaErrorInvalidValue;
 }

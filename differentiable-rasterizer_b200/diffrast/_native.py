@@ -75,7 +75,7 @@ SIGNATURES = {
     "dr_device_name": (_I, [_I, ctypes.c_char_p, ctypes.c_size_t]),
     "dr_device_count": (_I, []),
     "dr_set_background_location": (_I, [_P, _I]),
-    "dr_set_strict": (_I, [_P, _I]),
+    "dr_set_precision": (_I, [_P, _I]),
     "dr_render": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "dr_loss_backward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P, _P]),
     "dr_grad_backward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P]),
@@ -156,22 +156,27 @@ def context(device: torch.device, stream: int):
             if c is None:
                 h = _P()
                 check(lib().dr_ctx_create(device.index, ctypes.byref(h)))
-                if _strict:
-                    check(lib().dr_set_strict(h, 1))
+                if _precision != PRECISION_REFERENCE:
+                    check(lib().dr_set_precision(h, _precision))
                 _ctxs[key] = c = h
     return c
 
 
-_strict = False
+PRECISION_REFERENCE, PRECISION_STRICT, PRECISION_FAST = 0, 1, 2
+_precision = PRECISION_REFERENCE
 
 
-def set_strict(on: bool) -> None:
-    """Strict parity mode for every context (dr_set_strict)."""
-    global _strict
-    _strict = bool(on)
+def set_precision(mode: int) -> None:
+    """Soft-edge arithmetic for every context (dr_set_precision)."""
+    global _precision
+    _precision = int(mode)
     with _lock:
         for h in _ctxs.values():
-            check(lib().dr_set_strict(h, 1 if _strict else 0))
+            check(lib().dr_set_precision(h, _precision))
+
+
+def get_precision() -> int:
+    return _precision
 
 
 def shutdown() -> bool:

@@ -91,12 +91,24 @@ DR_API int dr_device_count(void);
 /* Where `background` pointers live: 0 = host memory (default), 1 = device. */
 DR_API dr_status dr_set_background_location(dr_ctx* ctx, int on_device);
 
-/* Strict parity mode (off by default). On: every soft-edge pixel evaluates the
- * reference's f32 expressions operation for operation (IEEE division and
- * sqrt, no contraction: raster.rs:96-134, grad.rs:231-270) instead of the fast
- * MUFU forms, at several times the cost. No reference counterpart (the
- * reference has a single precision mode); for bisecting parity questions. */
-DR_API dr_status dr_set_strict(dr_ctx* ctx, int strict);
+/* Arithmetic of soft-edge pixels (the band where 0 < coverage < 1).
+ *   DR_PRECISION_REFERENCE (default): the nearest edge's distance, the sigmoid
+ *     and the gradient direction follow the reference's f32 operations and
+ *     rounding (raster.rs:124-134, grad.rs:231-270). Within ~1e-5 of an edge
+ *     the reference's f32 gradient direction carries cancellation error of
+ *     ~1e-7/dist; this mode reproduces it, so results match the reference.
+ *   DR_PRECISION_STRICT: every edge with the reference's exact arithmetic
+ *     (IEEE division and sqrt throughout); slowest, for bisecting parity.
+ *   DR_PRECISION_FAST: closed-form shortcuts and approximate reciprocals;
+ *     closer to the exact (f64) gradient than the reference itself, but not
+ *     bit-compatible with its f32 rounding near edges.
+ * No reference counterpart (the reference has one precision). */
+typedef enum dr_precision {
+  DR_PRECISION_REFERENCE = 0,
+  DR_PRECISION_STRICT = 1,
+  DR_PRECISION_FAST = 2
+} dr_precision;
+DR_API dr_status dr_set_precision(dr_ctx* ctx, int precision);
 
 /* --- hot path ------------------------------------------------------------ */
 
