@@ -184,8 +184,6 @@ dr_status prepare(dr_ctx* ctx, const float* params, const float* background, int
   a.sigma_eff = std::fmax(sigma, 1e-8f);  // raster.rs:75 sigma.max(1e-8)
   a.inv_sigma = (float)(1.0 / (double)a.sigma_eff);
   a.precision = ctx->precision;
-  a.rej = kRejectSigmas * a.sigma_eff;
-  a.acc = kAcceptSigmas * a.sigma_eff;
   a.layout = layout;
   a.n_values = (double)H * (double)W * 3.0;
   a.grad_scale = 2.0f / (float)((long long)H * W * 3);  // grad.rs:112
@@ -615,8 +613,6 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       a.sigma_eff = std::fmax(sigma, 1e-8f);
       a.inv_sigma = (float)(1.0 / (double)a.sigma_eff);
       a.precision = ctx->precision;
-      a.rej = kRejectSigmas * a.sigma_eff;
-      a.acc = kAcceptSigmas * a.sigma_eff;
       a.bg3[0] = bg[0];
       a.bg3[1] = bg[1];
       a.bg3[2] = bg[2];

@@ -16,17 +16,9 @@ namespace dr {
 constexpr int kParams = 10;          // scene.rs:21 Triangle::N_PARAMS
 constexpr float kMinWeight = 1e-6f;  // raster.rs:34 MIN_WEIGHT
 
-// Fast-path thresholds in units of sigma. A pixel more than kRejectSigmas
-// outside an edge line has sigmoid(sd/sigma) < 5.0e-7, so w = alpha * cov is
-// below MIN_WEIGHT for every alpha <= 1 and the reference skips it. A pixel
-// more than kAcceptSigmas inside every edge line has exp(-sd/sigma) < 2.6e-8,
-// below half an f32 ulp of 1, so the reference's sigmoid rounds to exactly 1.0
-// and w == alpha; its vertex gradient is exactly zero (cov * (1 - cov) == 0).
-constexpr float kRejectSigmas = 14.5f;
-constexpr float kAcceptSigmas = 17.5f;
 
 // Triangle record written once per (scene, triangle) by the set-up kernel and
-// staged into shared memory by the raster kernels. 40 words, 16-byte aligned.
+// staged into shared memory by the raster kernels. 44 words, 16-byte aligned.
 struct __align__(16) TriRec {
   float v[6];     // x0 y0 x1 y1 x2 y2 (raw params)
   float e[6];     // edge vectors b - a for edges (v0,v1), (v1,v2), (v2,v0)
@@ -39,9 +31,12 @@ struct __align__(16) TriRec {
   int bbox[4];    // x0 y0 x1 y1 of pixel_bounds (raster.rs:144-168)
   int flags;
   float il[3];    // 1 / len2 (0 when len2 <= 1e-20: t = 0, raster.rs:129-130)
+  float rej;      // skip pixels with min edge-line distance below -rej
+  float acc;      // w == alpha for pixels with min edge-line distance above acc
+  float pad[2];
 };
-static_assert(sizeof(TriRec) == 160, "TriRec layout");
-constexpr int kRecWords = 40;
+static_assert(sizeof(TriRec) == 176, "TriRec layout");
+constexpr int kRecWords = 44;
 
 enum RecFlags : int {
   kLive = 1,         // has a non-empty box and a usable alpha

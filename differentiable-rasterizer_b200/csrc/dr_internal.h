@@ -21,7 +21,6 @@ struct RasterArgs {
   float sigma_eff;               // max(sigma, 1e-8) (raster.rs:75)
   float inv_sigma;               // 1 / sigma_eff
   int precision;                 // 0 reference rounding, 1 strict, 2 fast (band arithmetic)
-  float rej, acc;                // fast-path thresholds (normalized units)
   float bg3[3];                  // shared background when bg_dev is null
   const float* bg_dev;           // device background: 3 floats, or B*3 when bg_per_scene
   int bg_per_scene;

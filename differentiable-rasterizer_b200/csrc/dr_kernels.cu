@@ -150,6 +150,15 @@ __global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W,
   // Slack for evaluating n.p + c in f32 and for the reference's own f32
   // distance rounding: a few ulps of the largest magnitude involved.
   r.margin = (float)(4e-6 * (2.0 + maxabs));
+  // Pixels more than rej outside an edge line have w = alpha * cov below
+  // MIN_WEIGHT (cov <= exp(-dist/sigma) and alpha e^{-x} <= 1e-6 for
+  // x >= ln(alpha * 1e6); 0.2 of slack); pixels more than acc inside every
+  // edge line have exp(-x) below half an ulp of 1 (x > 16.64), so the
+  // reference's sigmoid rounds to exactly 1. Both include the margin.
+  const double sig_eff = fmax((double)sigma, 1e-8);
+  const double lna = alpha > 0.0f ? log((double)alpha * 1e6) : 0.0;
+  r.rej = (float)((fmax(lna, 0.0) + 0.2) * sig_eff) + r.margin;
+  r.acc = (float)(16.8 * sig_eff) + r.margin;
   for (int k = 0; k < 3; ++k) r.il[k] = r.len2[k] <= 1e-20f ? 0.0f : (float)(1.0 / (double)r.len2[k]);
   if (fast) flags |= kFastOk;
   r.flags = flags;
@@ -170,9 +179,9 @@ __global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W,
 // 4-bit code per warp block, decided once at binning time from the block's
 // rectangle against the triangle's box and edge lines:
 //   kBlkSkip    no pixel of the block can contribute (outside the box, or
-//               every pixel more than kRejectSigmas outside an edge line)
+//               every pixel more than the triangle's `rej` outside an edge)
 //   kBlkBox     the block straddles the box: test each pixel against it
-//   kBlkInside  every pixel is more than kAcceptSigmas inside every edge:
+//   kBlkInside  every pixel is more than the triangle's `acc` inside every edge:
 //               w == alpha exactly, no geometry
 // so whole warps skip or take the cheap path on a uniform branch.
 
@@ -190,7 +199,7 @@ struct Smem {
 // Block code of one warp block [bx0,bx1) x [by0,by1) (clipped to the image)
 // for one triangle record.
 __device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0, int bx1, int by1,
-                                              int W, int H, float rej, float acc) {
+                                              int W, int H) {
   if (bx0 >= bx1 || by0 >= by1) return kBlkSkip;
   const int x0 = r.bbox[0], y0 = r.bbox[1], x1 = r.bbox[2], y1 = r.bbox[3];
   if (bx1 <= x0 || bx0 >= x1 || by1 <= y0 || by0 >= y1) return kBlkSkip;
@@ -201,24 +210,23 @@ __device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0,
     const float inv_w = 1.0f / (float)W, inv_h = 1.0f / (float)H;
     const float cx = 0.5f * (float)(bx0 + bx1) * inv_w, hx = 0.5f * (float)(bx1 - bx0 - 1) * inv_w;
     const float cy = 0.5f * (float)(by0 + by1) * inv_h, hy = 0.5f * (float)(by1 - by0 - 1) * inv_h;
-    const float m = r.margin;
     float lmin_all = __int_as_float(0x7f800000);
 #pragma unroll
     for (int e = 0; e < 3; ++e) {
       const float nx = r.n[2 * e], ny = r.n[2 * e + 1];
       const float lc = __fmaf_rn(nx, cx, __fmaf_rn(ny, cy, r.c[e]));
       const float rad = __fmaf_rn(fabsf(nx), hx, __fmul_rn(fabsf(ny), hy));
-      if (__fadd_rn(lc, rad) < -(rej + m)) return kBlkSkip;
+      if (__fadd_rn(lc, rad) < -r.rej) return kBlkSkip;
       lmin_all = fminf(lmin_all, __fsub_rn(lc, rad));
     }
-    if (lmin_all > acc + m) code = kBlkInside;  // deep inside implies inside the box
+    if (lmin_all > r.acc) code = kBlkInside;  // deep inside implies inside the box
   }
   return code;
 }
 
 // Bin triangles [c0, c0 + kChunk) of one scene against the tile, in order.
 __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int c0, int tx0,
-                          int ty0, int W, int H, float rej, float acc) {
+                          int ty0, int W, int H) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k = c0 + (int)threadIdx.x;
   bool keep = false;
@@ -231,7 +239,7 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
     for (int wb = 0; wb < kWarps; ++wb) {
       const int bx0 = tx0 + (wb & 1) * kBlockW, by0 = ty0 + (wb >> 1) * kBlockH;
       const int c = classify_block(rr, bx0, by0, min(bx0 + kBlockW, W), min(by0 + kBlockH, H), W,
-                                   H, rej, acc);
+                                   H);
       code_all |= c << (4 * wb);
       skipped += (c & kBlkSkip) ? 1 : 0;
     }
@@ -261,7 +269,7 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
 }
 
 struct Consts {
-  float sigma_eff, inv_sigma, rej, acc;
+  float sigma_eff, inv_sigma;
 };
 
 // Precision modes of the soft-edge (band) arithmetic.
@@ -284,7 +292,7 @@ enum Prec : int { kPrecRef = 0, kPrecStrict = 1, kPrecFast = 2 };
 // (dbx, dby) for vertex `edge + 1` (grad.rs:264-268).
 struct PairEval {
   float w, cov;
-  bool band;
+  bool band, hit;
   float dax, day, dbx, dby;
   int edge;
 };
@@ -374,10 +382,16 @@ __device__ __forceinline__ void cov_grad_ref(const TriRec& r, int edge, float t,
 // inlining its IEEE divisions at every call site overflows the instruction
 // cache of the hot loop.
 template <bool kGrad>
-__device__ __noinline__ bool eval_ref(const TriRec& r, float ptx, float pty, const Consts& K,
-                                      PairEval& o) {
+__device__ __noinline__ PairEval eval_ref(const TriRec* rp, float ptx, float pty,
+                                          float sigma_eff) {
+  // Arguments and result by value: a reference to the caller's locals would
+  // force them (and every access in the hot loop) into local memory.
+  const TriRec& r = *rp;
+  PairEval o;
+  o.edge = 0;
+  o.dax = o.day = o.dbx = o.dby = 0.0f;
   const SdResult g = signed_distance_ref(r.v, r.e, r.len2, ptx, pty);
-  o.cov = sigmoid_ref(__fdiv_rn(g.sd, K.sigma_eff));
+  o.cov = sigmoid_ref(__fdiv_rn(g.sd, sigma_eff));
   o.w = __fmul_rn(r.alpha, o.cov);
   o.band = !(g.dist < 1e-9f);
   if (kGrad && o.band) {
@@ -386,7 +400,7 @@ __device__ __noinline__ bool eval_ref(const TriRec& r, float ptx, float pty, con
     const float cpy = __fadd_rn(ay, __fmul_rn(g.t, r.e[2 * g.edge + 1]));
     const float ux = __fdiv_rn(__fsub_rn(ptx, cpx), g.dist);
     const float uy = __fdiv_rn(__fsub_rn(pty, cpy), g.dist);
-    float chain = __fdiv_rn(__fmul_rn(o.cov, __fsub_rn(1.0f, o.cov)), K.sigma_eff);
+    float chain = __fdiv_rn(__fmul_rn(o.cov, __fsub_rn(1.0f, o.cov)), sigma_eff);
     chain = (g.sd > 0.0f) ? chain : -chain;
     const float ka = __fmul_rn(chain, -__fsub_rn(1.0f, g.t));
     const float kb = __fmul_rn(chain, -g.t);
@@ -396,7 +410,8 @@ __device__ __noinline__ bool eval_ref(const TriRec& r, float ptx, float pty, con
     o.dby = __fmul_rn(kb, uy);
     o.edge = g.edge;
   }
-  return !(o.w <= kMinWeight);
+  o.hit = !(o.w <= kMinWeight);
+  return o;
 }
 
 // One pair, given the warp block's code. Returns kSkip (no contribution),
@@ -423,8 +438,8 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
   const float l1 = __fmaf_rn(r.n[2], ptx, __fmaf_rn(r.n[3], pty, r.c[1]));
   const float l2 = __fmaf_rn(r.n[4], ptx, __fmaf_rn(r.n[5], pty, r.c[2]));
   const float mn = fminf(fminf(l0, l1), l2);
-  if (mn < -(K.rej + r.margin)) return kSkip;
-  if (mn > K.acc + r.margin) {
+  if (mn < -r.rej) return kSkip;
+  if (mn > r.acc) {
     o.cov = 1.0f;
     o.w = r.alpha;
     o.band = false;
@@ -437,55 +452,47 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
   // from the reference's f32 decision; those rare pixels take the exact path.
   if (fabsf(mn) < r.margin) return kExact;
 
-  // Nearest edge. Inside a convex polygon the nearest boundary point is the
-  // foot on the nearest edge line (min_i l_i); outside it is the smallest
-  // clamped segment distance (raster.rs:124-134), a unique point.
+  // Nearest edge by clamped segment distance (raster.rs:124-134), the same
+  // computation inside and outside (inside, the nearest segment distance is
+  // the nearest edge-line distance), so no lane diverges on the side.
   const bool inside = mn >= 0.0f;
   int edge = 0;
-  float fdist = mn, ft = 0.0f, fdx = 0.0f, fdy = 0.0f, frs = 0.0f;
-  if (inside) {
-    float best = l0, second = __int_as_float(0x7f800000);
-    if (l1 < best) { second = best; best = l1; edge = 1; } else { second = l1; }
-    if (l2 < best) { second = best; edge = 2; } else { second = fminf(second, l2); }
-    if (second - best < r.margin) return kExact;
-  } else {
-    float bd2 = __int_as_float(0x7f800000), sd2 = bd2, st = 0.0f;
-    int sedge = 0;
+  float ft = 0.0f, fdx = 0.0f, fdy = 0.0f;
+  float bd2 = __int_as_float(0x7f800000), sd2 = bd2, st = 0.0f;
+  int sedge = 0;
 #pragma unroll
-    for (int e = 0; e < 3; ++e) {
-      const float ex = r.e[2 * e], ey = r.e[2 * e + 1];
-      const float apx = __fsub_rn(ptx, r.v[2 * e]), apy = __fsub_rn(pty, r.v[2 * e + 1]);
-      const float te = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[e]));
-      const float dx = __fmaf_rn(-te, ex, apx), dy = __fmaf_rn(-te, ey, apy);
-      const float d2 = __fmaf_rn(dx, dx, __fmul_rn(dy, dy));
-      if (d2 < bd2) {
-        sd2 = bd2;
-        st = ft;
-        sedge = edge;
-        bd2 = d2;
-        fdx = dx;
-        fdy = dy;
-        ft = te;
-        edge = e;
-      } else if (d2 < sd2) {
-        sd2 = d2;
-        st = te;
-        sedge = e;
-      }
+  for (int e = 0; e < 3; ++e) {
+    const float ex = r.e[2 * e], ey = r.e[2 * e + 1];
+    const float apx = __fsub_rn(ptx, r.v[2 * e]), apy = __fsub_rn(pty, r.v[2 * e + 1]);
+    const float te = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[e]));
+    const float dx = __fmaf_rn(-te, ex, apx), dy = __fmaf_rn(-te, ey, apy);
+    const float d2 = __fmaf_rn(dx, dx, __fmul_rn(dy, dy));
+    if (d2 < bd2) {
+      sd2 = bd2;
+      st = ft;
+      sedge = edge;
+      bd2 = d2;
+      fdx = dx;
+      fdy = dy;
+      ft = te;
+      edge = e;
+    } else if (d2 < sd2) {
+      sd2 = d2;
+      st = te;
+      sedge = e;
     }
-    frs = rsqrtf(bd2);
-    fdist = bd2 > 0.0f ? __fmul_rn(bd2, frs) : 0.0f;
-    // Two edges within rounding distance of each other (a sliver, or two
-    // nearly parallel edges) could be ordered differently by the reference's
-    // f32 distances, sending this pixel's gradient to another vertex pair:
-    // take the exact path. Adjacent edges both clamped to their shared
-    // vertex describe the same point and are not a real tie.
-    const bool same_vertex = (sedge == (edge + 1) % 3) ? (ft == 1.0f && st == 0.0f)
-                                                       : (ft == 0.0f && st == 1.0f);
-    if (!same_vertex &&
-        sd2 - bd2 < __fmul_rn(r.margin, __fmaf_rn(2.0f, fdist, r.margin)))
-      return kExact;
   }
+  const float frs = rsqrt_approx(bd2);
+  const float fdist = bd2 > 1e-30f ? __fmul_rn(bd2, frs) : 0.0f;
+  // Two edges within rounding distance of each other (an angle bisector
+  // inside, a sliver or nearly parallel edges outside) could be ordered
+  // differently by the reference's f32 distances, sending this pixel's
+  // gradient to another vertex pair: take the exact path. Adjacent edges both
+  // clamped to their shared vertex describe the same point: not a tie.
+  const bool same_vertex = (sedge == (edge + 1) % 3) ? (ft == 1.0f && st == 0.0f)
+                                                     : (ft == 0.0f && st == 1.0f);
+  if (!same_vertex && sd2 - bd2 < __fmul_rn(r.margin, __fmaf_rn(2.0f, fdist, r.margin)))
+    return kExact;
 
   if (kPrec == kPrecFast) {
     const float x = __fmul_rn(inside ? fdist : -fdist, K.inv_sigma);
@@ -493,17 +500,7 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
     o.w = __fmul_rn(r.alpha, o.cov);
     o.band = !(fdist < 1e-9f);
     if (kGrad && o.band) {
-      float t = ft, ux, uy;
-      if (inside) {
-        const float ex = r.e[2 * edge], ey = r.e[2 * edge + 1];
-        const float apx = __fsub_rn(ptx, r.v[2 * edge]), apy = __fsub_rn(pty, r.v[2 * edge + 1]);
-        t = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[edge]));
-        ux = r.n[2 * edge];
-        uy = r.n[2 * edge + 1];
-      } else {
-        ux = __fmul_rn(fdx, frs);
-        uy = __fmul_rn(fdy, frs);
-      }
+      const float t = ft, ux = __fmul_rn(fdx, frs), uy = __fmul_rn(fdy, frs);
       const float cov = o.cov;
       const float chain = __fmul_rn(__fmul_rn(cov, __fsub_rn(1.0f, cov)),
                                     inside ? K.inv_sigma : -K.inv_sigma);
@@ -665,7 +662,7 @@ __device__ __forceinline__ size_t pix_index(int layout, int b, int ch, int px, i
 }
 
 template <int Mode, int kPrec>
-__global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
+__global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   if (a.skip_flag && *a.skip_flag) return;
@@ -700,8 +697,6 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
   Consts K;
   K.sigma_eff = a.sigma_eff;
   K.inv_sigma = a.inv_sigma;
-  K.rej = a.rej;
-  K.acc = a.acc;
   const int n_chunks = (a.T + kChunk - 1) / kChunk;
   const int shift = 4 * warp;
 
@@ -717,7 +712,7 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
   }
   int count = 0;
   for (int ci = 0; ci < n_chunks; ++ci) {
-    count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H, K.rej, K.acc);
+    count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H);
     for (int j = 0; j < count; ++j) {
       const int code = (sm.bcode[j] >> shift) & 15;
       if (code & kBlkSkip) continue;
@@ -728,7 +723,10 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
         if (!active[q]) continue;
         PairEval pe;
         int st = eval_pair<false, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
-        if (st == kExact) st = eval_ref<false>(r, ptx, pty[q], K, pe) ? kHit : kSkip;
+        if (st == kExact) {
+          pe = eval_ref<false>(&r, ptx, pty[q], K.sigma_eff);
+          st = pe.hit ? kHit : kSkip;
+        }
         if (st == kSkip) continue;
         const float w = pe.w, om = __fsub_rn(1.0f, w);
         c0[q] = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(c0[q], om));  // raster.rs:63
@@ -791,7 +789,7 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
   for (int ci = 0; ci < n_chunks; ++ci) {
     if (n_chunks > 1) {
       __syncthreads();
-      count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H, K.rej, K.acc);
+      count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H);
     }
     for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
     __syncthreads();
@@ -809,7 +807,10 @@ __global__ void __launch_bounds__(kThreads) dr_raster_kernel(RasterArgs a) {
         if (!active[q]) continue;
         PairEval pe;
         int st = eval_pair<true, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
-        if (st == kExact) st = eval_ref<true>(r, ptx, pty[q], K, pe) ? kHit : kSkip;
+        if (st == kExact) {
+          pe = eval_ref<true>(&r, ptx, pty[q], K.sigma_eff);
+          st = pe.hit ? kHit : kSkip;
+        }
         if (st == kSkip) continue;
         contrib = true;
         const float w = pe.w, om = __fsub_rn(1.0f, w);
