@@ -17,7 +17,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = [os.path.join(CSRC, f) for f in ("dr_kernels.cu", "dr_capi.cu")]
+SOURCES = [os.path.join(CSRC, f) for f in ("dr_kernels.cu", "dr_capi.cu", "dr_noalloc.cu")]
 HEADERS = [
     os.path.join(CSRC, "dr_device.cuh"),
     os.path.join(CSRC, "dr_internal.h"),

@@ -81,6 +81,10 @@ struct Slot {
 
 }  // namespace
 
+namespace dr {
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace dr
+
 struct dr_ctx {
   int device = 0;
   std::mutex mu;

@@ -67,6 +67,8 @@ struct FitState {
 };
 
 size_t raster_smem_bytes();
+// Sets the calling thread's dr_last_error() message.
+void set_last_error(const char* msg);
 cudaError_t launch_fit_init(FitState* st, cudaStream_t s);
 cudaError_t launch_fit_control(FitState* st, int iter, float min_delta, long long patience,
                                float* losses, cudaStream_t s);

@@ -87,6 +87,8 @@ SIGNATURES = {
     "dr_fit": (
         _I, [_P, _P, _I, _I, _P, _P, _I, ctypes.POINTER(FitConfigC), _P, _P, _P,
              ctypes.POINTER(FitReportC), _P]),
+    "dr_loss_backward_noalloc": (
+        _I, [_P, _P, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P]),
     "dr_pool_stats_get": (_I, [_P, ctypes.POINTER(PoolStatsC)]),
     "dr_clear_pool": (_I, [_P]),
     "dr_stream_wait": (_I, [_P, ctypes.c_double]),

@@ -204,6 +204,29 @@ DR_API dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const fl
                  const float* background, int T, const dr_fit_config* cfg, float* best_params,
                  float* final_params, float* losses, dr_fit_report* report, dr_stream_t stream);
 
+/* dr_loss_backward with no device allocation: no context, no cudaMalloc, no
+ * cudaFree. No counterpart in the reference. For callers that must not
+ * allocate on their hot path: cudaMalloc synchronizes the device and can stall
+ * for milliseconds (fatal to frame- or deadline-bound loops), and some hosts
+ * hand out device memory only from their own fixed budget. Scratch comes from
+ * one static array compiled into the library (about 3.3 MB on every GPU that
+ * loads it, held until exit), so a call is limited to B*T <=
+ * DR_NOALLOC_MAX_TRIANGLES, B <= DR_NOALLOC_MAX_BATCH and
+ * B * ceil(H/16) * ceil(W/16) <= DR_NOALLOC_MAX_TILES (DR_TOO_LARGE beyond).
+ * Runs on the current device and `stream`; background is 3 host floats (or
+ * NULL for black), shared by the batch; precision is the default. The first
+ * call on each device sets up the array's address: make it before any stream
+ * capture. All calls share the array, so calls that could overlap on the GPU
+ * race: serialize them. Outputs as dr_loss_backward (grads overwritten, losses
+ * may be NULL). */
+#define DR_NOALLOC_MAX_TRIANGLES 16384
+#define DR_NOALLOC_MAX_BATCH 1024
+#define DR_NOALLOC_MAX_TILES 65536
+DR_API dr_status dr_loss_backward_noalloc(const float* params, const float* background, int B,
+                                          int T, int H, int W, float sigma, const float* targets,
+                                          int layout, float* grads, float* losses,
+                                          dr_stream_t stream);
+
 /* --- pool / sync ---------------------------------------------------------- */
 
 /* PoolStats (diffrast-gpu/src/lib.rs:153-158): scratch reuse counters. */
