@@ -1,0 +1,82 @@
+"""One large scene split across GPUs by tile rows.
+
+Each rank renders and differentiates only the 16-pixel tile rows
+``r % world == rank`` (``dr_loss_backward_sharded``): image rows are disjoint,
+so the forward needs no communication. The ranks then all-reduce one buffer
+holding the partial T x 10 gradient and the partial f64 sum of squared error,
+and every rank applies the same Adam step, so the parameters stay identical
+without a broadcast. The reference has no multi-device path; the sum over
+shards equals the single-device ``dr_loss_backward`` (tested).
+
+One process per GPU, ``torch.distributed`` with the NCCL backend for the
+all-reduce (gloo works too, for CPU-side tests of the plumbing).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native
+
+TILE = 16
+
+
+def shard_rows(height: int, shard: int, n_shards: int) -> list[int]:
+    """Tile rows a shard covers: every n-th 16-pixel row, interleaved so that
+    bands of dense geometry spread over all ranks."""
+    if not (0 <= shard < n_shards):
+        raise ValueError(f"shard {shard} of {n_shards}")
+    tiles_y = (height + TILE - 1) // TILE
+    return list(range(shard, tiles_y, n_shards))
+
+
+def pack_for_reduce(grads: torch.Tensor, loss_sums: torch.Tensor) -> torch.Tensor:
+    """One f64 buffer [grads..., loss sums...] so a single collective carries both
+    (summing the partial gradients in f64 also removes the f32 order noise)."""
+    return torch.cat([grads.reshape(-1).to(torch.float64), loss_sums.reshape(-1)])
+
+
+def unpack_reduced(buf: torch.Tensor, grads_shape, batch: int):
+    n = buf.numel() - batch
+    grads = buf[:n].to(torch.float32).reshape(grads_shape)
+    return grads, buf[n:]
+
+
+class ShardedSceneStep:
+    """Forward + MSE + backward of one (or a few) large scenes across ranks, then
+    Adam with the fit's per-parameter rates and projection (fit.rs:388-424)."""
+
+    def __init__(self, params: torch.Tensor, group=None, lr_pos=0.004, lr_color=0.02,
+                 lr_alpha=0.01):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if params.dim() != 3 or params.shape[-1] != _native.N_PARAMS:
+            raise ValueError("params must be (B, T, 10)")
+        self.params = params.detach().to(torch.float32).contiguous()
+        self.m = torch.zeros_like(self.params)
+        self.v = torch.zeros_like(self.params)
+        self.t = 0
+        self.lrs = (lr_pos, lr_color, lr_alpha)
+
+    def loss_and_grads(self, targets: torch.Tensor, sigma: float, background=(0.0, 0.0, 0.0)):
+        """All-reduced (losses (B,), grads (B, T, 10)) for the current params."""
+        sums, grads = _native.loss_backward_sharded(self.params, targets, sigma, self.rank,
+                                                    self.world, background)
+        buf = pack_for_reduce(grads, sums)
+        if self.world > 1:
+            self.dist.all_reduce(buf, op=self.dist.ReduceOp.SUM, group=self.group)
+        grads, sums = unpack_reduced(buf, grads.shape, self.params.shape[0])
+        h, w = targets.shape[1], targets.shape[2]
+        losses = (sums / float(h * w * 3)).to(torch.float32)  # canvas.rs:58
+        return losses, grads
+
+    def step(self, targets: torch.Tensor, sigma: float, background=(0.0, 0.0, 0.0)):
+        """One fit iteration: loss, gradients, Adam + projection. Returns losses."""
+        losses, grads = self.loss_and_grads(targets, sigma, background)
+        self.t += 1
+        _native.adam_step(self.params, self.m, self.v, grads.contiguous(), self.t, *self.lrs)
+        return losses
