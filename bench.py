@@ -52,10 +52,11 @@ FLOP_PER_PAIR = 170  # fwd 62 + bwd 108 FP32 FLOP per bounding-box pair
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fit", action="store_true", help="skip the secondary fit metric")
     return ap.parse_args()
 
 
@@ -158,6 +159,49 @@ def cpu_reference_rate(params, target, threads: int = 0, max_scenes: int = B):
     oracle.backward_batch(p, t, SIGMA, threads=threads)
     dt = time.perf_counter() - t0
     return dense_pairs(p.shape[0]) / dt, dt, p.shape[0]
+
+
+def fit_metric(dev, with_cpu: bool):
+    """Secondary BASELINE metric: Adam fit iterations/s on config 1 (150
+    triangles fitted to a 176x176 target for 800 iterations, FitConfig
+    defaults), the whole loop on the device (dr_fit, one CUDA graph)."""
+    import torch
+
+    import oracle
+    from diffrast import _native
+    from diffrast.scenes import config1_target_scene, seed_scene_geometry
+
+    oracle.build()
+    target = oracle.render_batch(config1_target_scene(150, 0), 176, 176, 0.0015)[0]
+    p = seed_scene_geometry(150, 1)
+    bg = oracle.seed_colors(target, p)
+    t_dev = torch.from_numpy(target).to(dev)
+    p_dev = torch.from_numpy(p).to(dev)
+    kw = dict(iters=800, patience=None)
+    _native.fit(t_dev, p_dev, [float(v) for v in bg], **kw)  # capture + warm-up
+    torch.cuda.synchronize(dev)
+    reps = 3
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        rep = _native.fit(t_dev, p_dev, [float(v) for v in bg], **kw)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dt = e0.elapsed_time(e1) / 1e3 / reps
+    out = {"metric": "Adam fit iters/s (config 1: T=150, 176x176, 800 iters)",
+           "value": len(rep["losses"]) / dt, "unit": "iters/s",
+           "timing": "CUDA events around dr_fit (one graph launch per 800-iteration fit)",
+           "final_best_loss": rep["best_loss"]}
+    if with_cpu:
+        t0 = time.perf_counter()
+        r = oracle.fit(target, p, bg, oracle.FitConfig(iters=200, patience=None))
+        cdt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": len(r.losses) / cdt, "unit": "iters/s", "cores": 1,
+                               "kind": "port", "sample": "first 200 of the 800 iterations, "
+                                                         "single thread (Fitter is sequential)"}
+    return out
 
 
 def run_reference(args, rank: int, world: int):
@@ -322,16 +366,18 @@ def main():
                          "timed": "whole step (set-up + raster kernels) per CUDA events"},
             "clocks": clock_info,
         }
+        if not args.no_fit:
+            line["secondary"] = fit_metric(dev, not args.no_cpu_baseline)
         if not args.no_cpu_baseline:
             import oracle
 
             tgt_np = target.cpu().numpy()
             thr = oracle.num_threads()
-            n_s = min(B, max(thr, 4))
-            rate, dt, ns = cpu_reference_rate(params_np, tgt_np, threads=thr, max_scenes=n_s)
+            rate, dt, ns = cpu_reference_rate(params_np, tgt_np, threads=thr, max_scenes=B)
             line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": thr, "kind": "port",
-                                    "sample": f"{ns} of the {B} scenes ({dt:.1f} s), "
-                                              "C++ restatement of the Rust CPU path"}
+                                    "sample": f"one full step ({ns} scenes, {dt:.1f} s wall on "
+                                              f"{thr} threads), C++ restatement of the Rust "
+                                              "CPU path"}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
