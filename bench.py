@@ -47,6 +47,7 @@ CELL = 5  # config 2 grid cell index for (T=128, 256^2)
 METRIC = "fwd+bwd pixel*triangle evals/s (B=32,T=128,256^2)"
 UNIT = "pair-evals/s"
 FLOP_PER_PAIR = 170  # fwd 62 + bwd 108 FP32 FLOP per bounding-box pair
+TRAFFIC_BYTES = 26_122_240  # DRAM bytes per raster launch (ncu, see roofline below)
 
 
 def parse():
@@ -359,7 +360,10 @@ def main():
                     "api": "diffrast.torch_layer.fused_loss on pinned CPU tensors"},
             "gpu_launches": 2 * args.steps,
             "roofline": {"bound": "fp32", "achieved": achieved, "peak": fp32_peak,
-                         "unit": "TFLOP/s", "frac": achieved / fp32_peak, "traffic": None,
+                         "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+                         # dram read + write of one raster launch, ncu capture in
+                         # profiles/raster_kernel_config2_b32_t128_256.md
+                         "traffic": TRAFFIC_BYTES,
                          "pairs_per_step": n_bbox, "flop_per_pair": FLOP_PER_PAIR,
                          "peak_source": f"nominal FP32 ({sms} SMs x 128 lanes x 2) at the "
                                         f"sampled SM clock {sm_mhz:.0f} MHz",
