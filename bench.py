@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 One step = one forward + per-image MSE + analytic backward over a batch of 32
-seeded synthetic scenes (BASELINE.json config 2's headline cell, sigma 0.0015),
+seeded synthetic scenes (benchmark config 2's headline cell, sigma 0.0015),
 through the C ABI (dr_loss_backward, the fused_loss_backward semantics). The
 metric counts dense pairs B*T*H*W per step, as the reference's own
 "fwd+bwd pixel*triangle evals/s" would.

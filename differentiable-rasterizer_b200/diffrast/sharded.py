@@ -1,4 +1,4 @@
-"""One large scene split across GPUs by tile rows.
+"""One large scene split across GPUs by tile rows (benchmark config 4).
 
 Each rank renders and differentiates only the 16-pixel tile rows
 ``r % world == rank`` (``dr_loss_backward_sharded``): image rows are disjoint,

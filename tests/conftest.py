@@ -40,7 +40,7 @@ def oracle():
     return o
 
 
-# --- tolerances of the north star ---------------------------
+# --- parity tolerances (images 1e-5 abs + 1e-4 rel, gradients 1e-6 + 1e-3 rel) --
 
 IMAGE_ATOL = 1e-5
 IMAGE_RTOL = 1e-4

@@ -70,7 +70,7 @@ def test_short_fit_tracks_the_oracle(native, oracle):
 
 
 def test_config1_fit(native, oracle):
-    # 150 triangles (seed 0, opacity U[0.3,1]) rendered
+    # Benchmark config 1: 150 triangles (seed 0, opacity U[0.3,1]) rendered
     # at 176x176 by the forward; fit from a seed-1 init, 800 iterations with
     # FitConfig defaults otherwise.
     from diffrast.scenes import config1_target_scene

@@ -241,7 +241,7 @@ def test_diffrast_rs_module_numpy_and_cuda_paths(oracle):
 
 
 def test_config3_torch_op_path(tl, oracle):
-    # B=256, T=64, 128^2, params = activate(randn(seed 2)),
+    # Benchmark config 3: B=256, T=64, 128^2, params = activate(randn(seed 2)),
     # targets = random_params(seed 3) rendered at sigma 0.0015;
     # F.mse_loss(rasterize(params), targets).backward() vs the CPU op.
     raw = torch.randn(256, 64, 10, generator=gen(2))

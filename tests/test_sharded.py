@@ -1,4 +1,4 @@
-"""Row-sharded single-scene path.
+"""Row-sharded single-scene path (benchmark config 4).
 
 CPU: the shard partition covers every tile row once, and the all-reduce
 plumbing gives every rank the same summed gradient (gloo, world size 2, with
