@@ -163,7 +163,7 @@ def cpu_reference_rate(params, target, threads: int = 0, max_scenes: int = B):
 
 
 def fit_metric(dev, with_cpu: bool):
-    """Secondary BASELINE metric: Adam fit iterations/s on config 1 (150
+    """Secondary benchmark metric: Adam fit iterations/s on config 1 (150
     triangles fitted to a 176x176 target for 800 iterations, FitConfig
     defaults), the whole loop on the device (dr_fit, one CUDA graph)."""
     import torch
