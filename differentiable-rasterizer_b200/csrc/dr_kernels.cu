@@ -36,7 +36,7 @@ constexpr int kPPT = DR_PPT;                             // pixels per thread (1
 constexpr int kBlockW = 8, kBlockH = 4 * kPPT;           // one warp's pixel block
 constexpr int kWarps = (kTile / kBlockW) * (kTile / kBlockH);
 constexpr int kThreads = kWarps * 32;
-static_assert(kWarps <= 8, "block codes pack 4 bits per warp into one int");
+static_assert(kWarps <= 8, "block codes are one byte per warp in one 64-bit word");
 constexpr int kChunk = 128;                              // triangles binned per round (<= kThreads)
 constexpr float kRenorm = 18446744073709551616.0f;        // 2^64
 constexpr float kRenormInv = 5.42101086242752217e-20f;    // 2^-64
@@ -183,12 +183,19 @@ __global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W,
 //   kBlkBox     the block straddles the box: test each pixel against it
 //   kBlkInside  every pixel is more than the triangle's `acc` inside every edge:
 //               w == alpha exactly, no geometry
-// so whole warps skip or take the cheap path on a uniform branch.
+// so whole warps skip or take the cheap path on a uniform branch. Bits 3-5
+// of the code mark the edges that can be the nearest edge of a contributing
+// pixel of the block (the candidates): an edge whose line stays farther than
+// max(rej, acc) from every pixel of the block is farther than that from the
+// pixel as a segment too, while a contributing pixel's nearest edge is within
+// rej (outside) or acc (inside, where nearest segment = nearest line). Most
+// soft-edge blocks have a single candidate, which fixes the nearest edge for
+// the whole warp.
 
-constexpr int kBlkSkip = 1, kBlkBox = 2, kBlkInside = 4;
+constexpr int kBlkSkip = 1, kBlkBox = 2, kBlkInside = 4, kCandShift = 3;
 struct Smem {
   TriRec rec[kChunk];
-  int bcode[kChunk];
+  unsigned char bcode[kChunk][8];
   int kidx[kChunk];
   float acc[kChunk][kParams];
   int warp_count[kWarps];
@@ -210,7 +217,9 @@ __device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0,
     const float inv_w = 1.0f / (float)W, inv_h = 1.0f / (float)H;
     const float cx = 0.5f * (float)(bx0 + bx1) * inv_w, hx = 0.5f * (float)(bx1 - bx0 - 1) * inv_w;
     const float cy = 0.5f * (float)(by0 + by1) * inv_h, hy = 0.5f * (float)(by1 - by0 - 1) * inv_h;
+    const float thr = fmaxf(r.rej, r.acc) + r.margin;
     float lmin_all = __int_as_float(0x7f800000);
+    int cand = 0;
 #pragma unroll
     for (int e = 0; e < 3; ++e) {
       const float nx = r.n[2 * e], ny = r.n[2 * e + 1];
@@ -218,8 +227,12 @@ __device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0,
       const float rad = __fmaf_rn(fabsf(nx), hx, __fmul_rn(fabsf(ny), hy));
       if (__fadd_rn(lc, rad) < -r.rej) return kBlkSkip;
       lmin_all = fminf(lmin_all, __fsub_rn(lc, rad));
+      if (!(__fsub_rn(fabsf(lc), rad) > thr)) cand |= 1 << e;
     }
-    if (lmin_all > r.acc) code = kBlkInside;  // deep inside implies inside the box
+    if (lmin_all > r.acc) return kBlkInside;  // deep inside implies inside the box
+    code |= cand << kCandShift;
+  } else {
+    code |= 7 << kCandShift;
   }
   return code;
 }
@@ -230,7 +243,7 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int k = c0 + (int)threadIdx.x;
   bool keep = false;
-  int code_all = 0;
+  unsigned long long code_all = 0;
   const TriRec* r = recs + k;
   if ((int)threadIdx.x < kChunk && k < T && (r->flags & kLive)) {
     const TriRec& rr = *r;
@@ -240,7 +253,7 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
       const int bx0 = tx0 + (wb & 1) * kBlockW, by0 = ty0 + (wb >> 1) * kBlockH;
       const int c = classify_block(rr, bx0, by0, min(bx0 + kBlockW, W), min(by0 + kBlockH, H), W,
                                    H);
-      code_all |= c << (4 * wb);
+      code_all |= (unsigned long long)c << (8 * wb);
       skipped += (c & kBlkSkip) ? 1 : 0;
     }
     keep = skipped < kWarps;
@@ -258,7 +271,7 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
   if (keep) {
     const int slot = base + __popc(ballot & ((1u << lane) - 1u));
     sm.kidx[slot] = k;
-    sm.bcode[slot] = code_all;
+    *reinterpret_cast<unsigned long long*>(sm.bcode[slot]) = code_all;
     const float4* src = reinterpret_cast<const float4*>(r);
     float4* dst = reinterpret_cast<float4*>(&sm.rec[slot]);
 #pragma unroll
@@ -434,9 +447,13 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
     return kHit;  // alpha > MIN_WEIGHT is guaranteed by the set-up cull
   }
   if (!(r.flags & kFastOk)) return kExact;
-  const float l0 = __fmaf_rn(r.n[0], ptx, __fmaf_rn(r.n[1], pty, r.c[0]));
-  const float l1 = __fmaf_rn(r.n[2], ptx, __fmaf_rn(r.n[3], pty, r.c[1]));
-  const float l2 = __fmaf_rn(r.n[4], ptx, __fmaf_rn(r.n[5], pty, r.c[2]));
+  // Edges that are not candidates lie farther than max(rej, acc) on the inner
+  // side of every pixel of the block: they take no part in any decision.
+  const int cand = code >> kCandShift;
+  const float inf = __int_as_float(0x7f800000);
+  const float l0 = (cand & 1) ? __fmaf_rn(r.n[0], ptx, __fmaf_rn(r.n[1], pty, r.c[0])) : inf;
+  const float l1 = (cand & 2) ? __fmaf_rn(r.n[2], ptx, __fmaf_rn(r.n[3], pty, r.c[1])) : inf;
+  const float l2 = (cand & 4) ? __fmaf_rn(r.n[4], ptx, __fmaf_rn(r.n[5], pty, r.c[2])) : inf;
   const float mn = fminf(fminf(l0, l1), l2);
   if (mn < -r.rej) return kSkip;
   if (mn > r.acc) {
@@ -462,6 +479,7 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
   int sedge = 0;
 #pragma unroll
   for (int e = 0; e < 3; ++e) {
+    if (!(cand & (1 << e))) continue;
     const float ex = r.e[2 * e], ey = r.e[2 * e + 1];
     const float apx = __fsub_rn(ptx, r.v[2 * e]), apy = __fsub_rn(pty, r.v[2 * e + 1]);
     const float te = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[e]));
@@ -535,6 +553,50 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
   return o.w <= kMinWeight ? kSkip : kHit;
 }
 
+// One pair of a block with a single candidate edge `e` (reference precision).
+// Within such a block every other edge line lies more than max(rej, acc) on
+// the inner side of the pixel, so the pixel is inside exactly when it is on
+// the inner side of edge e, and for every pixel that composites (outside:
+// nearest distance below rej; inside: below acc, else cov == 1) edge e is the
+// reference's nearest edge, with a margin far above rounding. Only edge e's
+// segment distance is computed, with the reference's operations. Vertex
+// gradients are returned for vertices e and e + 1 (pe.edge == e).
+template <bool kGrad>
+__device__ __forceinline__ int eval_single(const TriRec& r, int code, int e, int px, int py,
+                                           float ptx, float pty, const Consts& K, PairEval& o) {
+  if (code & kBlkBox) {
+    if (px < r.bbox[0] || px >= r.bbox[2] || py < r.bbox[1] || py >= r.bbox[3]) return kSkip;
+  }
+  const float l = __fmaf_rn(r.n[2 * e], ptx, __fmaf_rn(r.n[2 * e + 1], pty, r.c[e]));
+  if (l < -r.rej) return kSkip;
+  if (l > r.acc) {
+    o.cov = 1.0f;
+    o.w = r.alpha;
+    o.band = false;
+    return kHit;
+  }
+  if (fabsf(l) < r.margin) return kExact;
+  const bool inside = l >= 0.0f;
+  // point_segment_distance (raster.rs:124-134) for edge e.
+  const float ax = r.v[2 * e], ay = r.v[2 * e + 1];
+  const float ex = r.e[2 * e], ey = r.e[2 * e + 1], len2 = r.len2[e];
+  const float apx = __fsub_rn(ptx, ax), apy = __fsub_rn(pty, ay);
+  float t = 0.0f;
+  if (!(len2 <= 1e-20f)) {
+    const float dot = __fadd_rn(__fmul_rn(apx, ex), __fmul_rn(apy, ey));
+    t = rclamp(div_rn_inv(dot, len2, r.il[e]), 0.0f, 1.0f);
+  }
+  const float dx = __fsub_rn(apx, __fmul_rn(t, ex));
+  const float dy = __fsub_rn(apy, __fmul_rn(t, ey));
+  const float dist = sqrt_nr(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)));
+  const float sd = inside ? dist : -dist;
+  o.cov = sigmoid_rounded(div_rn_inv(sd, K.sigma_eff, K.inv_sigma));
+  o.w = __fmul_rn(r.alpha, o.cov);
+  o.band = !(dist < 1e-9f);
+  if (kGrad && o.band) cov_grad_ref(r, e, t, dist, o.cov, inside, ptx, pty, K, o);
+  return o.w <= kMinWeight ? kSkip : kHit;
+}
+
 // Running product of (1 - w) with 2^64 renormalisation and barrier tracking.
 struct Prod {
   float m;
@@ -548,20 +610,17 @@ struct Prod {
     zn = -1;
   }
   __device__ __forceinline__ void mul(float f, int k) {
-    if (f == 0.0f) {
-      z0 = k;
-      m = 1.0f;
-      e = 0;
-    } else if (f != f) {
-      zn = k;
-      m = 1.0f;
-      e = 0;
-    } else {
+    if (f > 0.0f) {  // f = 1 - w lies in [0, 1) or is NaN
       m = __fmul_rn(m, f);
       if (m < kRenormInv) {
         m = __fmul_rn(m, kRenorm);
         e += 1;
       }
+    } else {
+      if (f == 0.0f) z0 = k;
+      else zn = k;
+      m = 1.0f;
+      e = 0;
     }
   }
 };
@@ -569,12 +628,13 @@ struct Prod {
 // A_k = prod over layers above k of (1 - w), from the full product P (after
 // the last layer) and the running product Q (through layer k). A barrier
 // layer resets Q to 1, so the same ratio yields the product above it.
-template <int kPrec>
+// The reference attenuates by a running product in the opposite order, so
+// the ratio matches it to rounding only and needs no exact division: both
+// mantissas lie in [2^-64, 1], where the approximate quotient is within 2 ulp.
 __device__ __forceinline__ float attenuation(const Prod& P, const Prod& Q, int k) {
   if (k < P.zn) return __int_as_float(0x7fc00000);
   if (k < P.z0) return 0.0f;
-  const float ratio =
-      kPrec == kPrecFast ? __fdividef(P.m, Q.m) : div_rn_inv(P.m, Q.m, rcp_nr(Q.m));
+  const float ratio = __fdividef(P.m, Q.m);
   const int de = P.e - Q.e;
   if (de == 0) return ratio;
   if (de == 1) return __fmul_rn(ratio, kRenormInv);
@@ -655,6 +715,44 @@ __device__ __forceinline__ float reduce4(float v0, float v1, float v2, float v3,
   return k;
 }
 
+// 8 values: lanes with (lane & 3) == 0 hold the total of value
+// 4 * bit4 + 2 * bit3 + bit2 of the lane index (9 shuffles).
+__device__ __forceinline__ float reduce8(const float (&v)[8], int lane) {
+  const unsigned F = 0xffffffffu;
+  bool h = lane & 16;
+  float a[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float keep = h ? v[4 + i] : v[i];
+    const float send = h ? v[i] : v[4 + i];
+    a[i] = keep + __shfl_xor_sync(F, send, 16);
+  }
+  h = lane & 8;
+  float b[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float keep = h ? a[2 + i] : a[i];
+    const float send = h ? a[i] : a[2 + i];
+    b[i] = keep + __shfl_xor_sync(F, send, 8);
+  }
+  h = lane & 4;
+  float c = (h ? b[1] : b[0]) + __shfl_xor_sync(F, h ? b[0] : b[1], 4);
+  c += __shfl_xor_sync(F, c, 2);
+  c += __shfl_xor_sync(F, c, 1);
+  return c;
+}
+
+// Which entry of (a_x, a_y, b_x, b_y, r, g, b, alpha) a lane holds after
+// reduce8, as a parameter index for a single-edge entry with edge e
+// (a = vertex e, b = vertex e + 1); -1 for lanes that hold no total.
+__device__ __forceinline__ int reduce8_param(int lane, int e) {
+  if (lane & 3) return -1;
+  const int s = lane >> 2;  // 4 * bit4 + 2 * bit3 + bit2
+  if (s >= 4) return 6 + (s - 4);
+  const int vtx = (s < 2) ? e : (e == 2 ? 0 : e + 1);
+  return 2 * vtx + (s & 1);
+}
+
 __device__ __forceinline__ size_t pix_index(int layout, int b, int ch, int px, int py, int W,
                                             int H) {
   if (layout == kLayoutBCHW) return (((size_t)b * 3 + ch) * H + py) * W + px;
@@ -698,7 +796,6 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   K.sigma_eff = a.sigma_eff;
   K.inv_sigma = a.inv_sigma;
   const int n_chunks = (a.T + kChunk - 1) / kChunk;
-  const int shift = 4 * warp;
 
   // ---- pass 1: forward composite ------------------------------------------
   float c0[kPPT], c1[kPPT], c2[kPPT];
@@ -714,15 +811,26 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   for (int ci = 0; ci < n_chunks; ++ci) {
     count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H);
     for (int j = 0; j < count; ++j) {
-      const int code = (sm.bcode[j] >> shift) & 15;
+      const int code = sm.bcode[j][warp];
       if (code & kBlkSkip) continue;
       const TriRec& r = sm.rec[j];
       const int k = sm.kidx[j];
+      const int cand = code >> kCandShift;
+      const bool single = kPrec == kPrecRef && (cand & (cand - 1)) == 0;
+      const int e1 = cand - 1 - (cand >> 2);  // the single candidate: 1, 2, 4 -> 0, 1, 2
 #pragma unroll
       for (int q = 0; q < kPPT; ++q) {
         if (!active[q]) continue;
         PairEval pe;
-        int st = eval_pair<false, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
+        int st;
+        if (code & kBlkInside) {
+          pe.w = r.alpha;
+          st = kHit;
+        } else if (single) {
+          st = eval_single<false>(r, code, e1, px, py[q], ptx, pty[q], K, pe);
+        } else {
+          st = eval_pair<false, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
+        }
         if (st == kExact) {
           pe = eval_ref<false>(&r, ptx, pty[q], K.sigma_eff);
           st = pe.hit ? kHit : kSkip;
@@ -794,10 +902,15 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
     __syncthreads();
     for (int j = 0; j < count; ++j) {
-      const int code = (sm.bcode[j] >> shift) & 15;
+      const int code = sm.bcode[j][warp];
       if (code & kBlkSkip) continue;
       const TriRec& r = sm.rec[j];
       const int k = sm.kidx[j];
+      const int cand = code >> kCandShift;
+      // Single-edge entries accumulate vertex gradients relative to the edge
+      // (acc[0..3] = vertex e, vertex e + 1), others by vertex (acc[0..5]).
+      const bool single = kPrec == kPrecRef && !(code & kBlkInside) && (cand & (cand - 1)) == 0;
+      const int e1 = cand - 1 - (cand >> 2);
       float acc[10];
 #pragma unroll
       for (int i = 0; i < 10; ++i) acc[i] = 0.0f;
@@ -806,7 +919,17 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
       for (int q = 0; q < kPPT; ++q) {
         if (!active[q]) continue;
         PairEval pe;
-        int st = eval_pair<true, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
+        int st;
+        if (code & kBlkInside) {
+          pe.w = r.alpha;
+          pe.cov = 1.0f;
+          pe.band = false;
+          st = kHit;
+        } else if (single) {
+          st = eval_single<true>(r, code, e1, px, py[q], ptx, pty[q], K, pe);
+        } else {
+          st = eval_pair<true, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
+        }
         if (st == kExact) {
           pe = eval_ref<true>(&r, ptx, pty[q], K.sigma_eff);
           st = pe.hit ? kHit : kSkip;
@@ -815,7 +938,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
         contrib = true;
         const float w = pe.w, om = __fsub_rn(1.0f, w);
         Q[q].mul(om, k);
-        const float A = attenuation<kPrec>(P[q], Q[q], k);
+        const float A = attenuation(P[q], Q[q], k);
         const float g0 = __fmul_rn(G0[q], A), g1 = __fmul_rn(G1[q], A), g2 = __fmul_rn(G2[q], A);
         // grad.rs:162-179
         acc[6] = __fmaf_rn(g0, w, acc[6]);
@@ -832,13 +955,22 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
           const float d_cov = __fmul_rn(d_w, r.alpha);
           const float ax = __fmul_rn(d_cov, pe.dax), ay = __fmul_rn(d_cov, pe.day);
           const float bx = __fmul_rn(d_cov, pe.dbx), by = __fmul_rn(d_cov, pe.dby);
-          const int e = pe.edge;
-          acc[0] += (e == 0) ? ax : ((e == 2) ? bx : 0.0f);
-          acc[1] += (e == 0) ? ay : ((e == 2) ? by : 0.0f);
-          acc[2] += (e == 1) ? ax : ((e == 0) ? bx : 0.0f);
-          acc[3] += (e == 1) ? ay : ((e == 0) ? by : 0.0f);
-          acc[4] += (e == 2) ? ax : ((e == 1) ? bx : 0.0f);
-          acc[5] += (e == 2) ? ay : ((e == 1) ? by : 0.0f);
+          if (single) {
+            // An exact-path pixel of a single-edge block that composites has
+            // edge e as its nearest edge too (see eval_single).
+            acc[0] += ax;
+            acc[1] += ay;
+            acc[2] += bx;
+            acc[3] += by;
+          } else {
+            const int e = pe.edge;
+            acc[0] += (e == 0) ? ax : ((e == 2) ? bx : 0.0f);
+            acc[1] += (e == 0) ? ay : ((e == 2) ? by : 0.0f);
+            acc[2] += (e == 1) ? ax : ((e == 0) ? bx : 0.0f);
+            acc[3] += (e == 1) ? ay : ((e == 0) ? by : 0.0f);
+            acc[4] += (e == 2) ? ax : ((e == 1) ? bx : 0.0f);
+            acc[5] += (e == 2) ? ay : ((e == 1) ? by : 0.0f);
+          }
         }
         r0[q] = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(r0[q], om));  // raster.rs:63
         r1[q] = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(r1[q], om));
@@ -848,8 +980,15 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
       const unsigned any = __ballot_sync(0xffffffffu, contrib);
       if (any == 0u) continue;
       if (__any_sync(0xffffffffu, band)) {
-        const float s = reduce10(acc, lane);
-        if (slot10 >= 0) atomicAdd(&sm.acc[j][slot10], s);
+        if (single) {
+          const float v8[8] = {acc[0], acc[1], acc[2], acc[3], acc[6], acc[7], acc[8], acc[9]};
+          const float s = reduce8(v8, lane);
+          const int prm = reduce8_param(lane, e1);
+          if (prm >= 0) atomicAdd(&sm.acc[j][prm], s);
+        } else {
+          const float s = reduce10(acc, lane);
+          if (slot10 >= 0) atomicAdd(&sm.acc[j][slot10], s);
+        }
       } else {
         const float s = reduce4(acc[6], acc[7], acc[8], acc[9], lane);
         if ((lane & 7) == 0) atomicAdd(&sm.acc[j][6 + (lane >> 3)], s);
