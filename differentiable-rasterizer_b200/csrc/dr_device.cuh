@@ -33,7 +33,9 @@ struct __align__(16) TriRec {
   float il[3];    // 1 / len2 (0 when len2 <= 1e-20: t = 0, raster.rs:129-130)
   float rej;      // skip pixels with min edge-line distance below -rej
   float acc;      // w == alpha for pixels with min edge-line distance above acc
-  float pad[2];
+  float wind;     // sign of the signed area (+1 / -1): the sign of the reference's
+                  // edge cross product on the inner side of every edge
+  float pad;
 };
 static_assert(sizeof(TriRec) == 176, "TriRec layout");
 constexpr int kRecWords = 44;

@@ -160,6 +160,8 @@ __global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W,
   r.rej = (float)((fmax(lna, 0.0) + 0.2) * sig_eff) + r.margin;
   r.acc = (float)(16.8 * sig_eff) + r.margin;
   for (int k = 0; k < 3; ++k) r.il[k] = r.len2[k] <= 1e-20f ? 0.0f : (float)(1.0 / (double)r.len2[k]);
+  r.wind = (float)s;
+  r.pad = 0.0f;
   if (fast) flags |= kFastOk;
   r.flags = flags;
 
@@ -553,48 +555,75 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
   return o.w <= kMinWeight ? kSkip : kHit;
 }
 
-// One pair of a block with a single candidate edge `e` (reference precision).
-// Within such a block every other edge line lies more than max(rej, acc) on
-// the inner side of the pixel, so the pixel is inside exactly when it is on
-// the inner side of edge e, and for every pixel that composites (outside:
-// nearest distance below rej; inside: below acc, else cov == 1) edge e is the
-// reference's nearest edge, with a margin far above rounding. Only edge e's
-// segment distance is computed, with the reference's operations. Vertex
-// gradients are returned for vertices e and e + 1 (pe.edge == e).
-template <bool kGrad>
-__device__ __forceinline__ int eval_single(const TriRec& r, int code, int e, int px, int py,
-                                           float ptx, float pty, const Consts& K, PairEval& o) {
-  if (code & kBlkBox) {
-    if (px < r.bbox[0] || px >= r.bbox[2] || py < r.bbox[1] || py >= r.bbox[3]) return kSkip;
-  }
-  const float l = __fmaf_rn(r.n[2 * e], ptx, __fmaf_rn(r.n[2 * e + 1], pty, r.c[e]));
-  if (l < -r.rej) return kSkip;
-  if (l > r.acc) {
-    o.cov = 1.0f;
-    o.w = r.alpha;
-    o.band = false;
-    return kHit;
-  }
-  if (fabsf(l) < r.margin) return kExact;
-  const bool inside = l >= 0.0f;
-  // point_segment_distance (raster.rs:124-134) for edge e.
-  const float ax = r.v[2 * e], ay = r.v[2 * e + 1];
+// One edge's point_segment_distance (raster.rs:124-134) and winding cross
+// product (raster.rs:119-122) with the reference's operations and rounding.
+struct SegEval {
+  float d, t, cross;
+};
+__device__ __forceinline__ SegEval seg_exact(const TriRec& r, int e, float ptx, float pty) {
   const float ex = r.e[2 * e], ey = r.e[2 * e + 1], len2 = r.len2[e];
-  const float apx = __fsub_rn(ptx, ax), apy = __fsub_rn(pty, ay);
-  float t = 0.0f;
-  if (!(len2 <= 1e-20f)) {
-    const float dot = __fadd_rn(__fmul_rn(apx, ex), __fmul_rn(apy, ey));
-    t = rclamp(div_rn_inv(dot, len2, r.il[e]), 0.0f, 1.0f);
+  const float apx = __fsub_rn(ptx, r.v[2 * e]), apy = __fsub_rn(pty, r.v[2 * e + 1]);
+  const float dot = __fadd_rn(__fmul_rn(apx, ex), __fmul_rn(apy, ey));
+  SegEval o;
+  o.t = len2 <= 1e-20f ? 0.0f : rclamp(div_rn_inv(dot, len2, r.il[e]), 0.0f, 1.0f);
+  const float dx = __fsub_rn(apx, __fmul_rn(o.t, ex));
+  const float dy = __fsub_rn(apy, __fmul_rn(o.t, ey));
+  o.d = sqrt_nr(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)));
+  o.cross = __fsub_rn(__fmul_rn(ex, apy), __fmul_rn(ey, apx));
+  return o;
+}
+
+// Soft-edge value of one pair for reference precision, from the candidate
+// edges of the pixel's warp block (`cand`, at least one bit). A non-candidate
+// edge's line lies more than max(rej, acc) on the inner side of every pixel of
+// the block, so:
+//  - it is not the reference's nearest edge of any pixel that composites
+//    (outside, that edge is nearer than rej; inside, nearer than acc, or
+//    cov == 1 exactly), and
+//  - its cross product has the sign of the winding, so is_inside
+//    (raster.rs:111-122) is decided by the candidates' own cross products.
+// Each candidate's distance and cross product are the reference's f32 values,
+// and the nearest edge is chosen by the reference's strict `<` in edge order
+// (grad.rs:236-242), so ties resolve as the reference resolves them. Pixels
+// farther than rej outside, or farther than acc inside every candidate line,
+// take the box tests' answers (skip; cov == 1). Degenerate triangles and NaN
+// alpha return kExact.
+template <bool kGrad>
+__device__ __forceinline__ int eval_cand(const TriRec& r, int code, int cand, int px, int py,
+                                         float ptx, float pty, const Consts& K, PairEval& o) {
+  bool live = true;
+  if (code & kBlkBox) {
+    live = (px >= r.bbox[0]) & (px < r.bbox[2]) & (py >= r.bbox[1]) & (py < r.bbox[3]);
   }
-  const float dx = __fsub_rn(apx, __fmul_rn(t, ex));
-  const float dy = __fsub_rn(apy, __fmul_rn(t, ey));
-  const float dist = sqrt_nr(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)));
-  const float sd = inside ? dist : -dist;
-  o.cov = sigmoid_rounded(div_rn_inv(sd, K.sigma_eff, K.inv_sigma));
+  if (!(r.flags & kFastOk)) return live ? kExact : kSkip;
+  const float inf = __int_as_float(0x7f800000);
+  float mn = inf, best = inf, bt = 0.0f;
+  float cr[3];
+  int edge = 0;
+#pragma unroll
+  for (int e = 0; e < 3; ++e) {
+    cr[e] = r.wind;
+    if (!(cand & (1 << e))) continue;
+    mn = fminf(mn, __fmaf_rn(r.n[2 * e], ptx, __fmaf_rn(r.n[2 * e + 1], pty, r.c[e])));
+    const SegEval g = seg_exact(r, e, ptx, pty);
+    cr[e] = g.cross;
+    if (g.d < best) {
+      best = g.d;
+      bt = g.t;
+      edge = e;
+    }
+  }
+  live = live && !(mn < -r.rej);
+  const bool deep = mn > r.acc;
+  const bool inside = (cr[0] >= 0.0f && cr[1] >= 0.0f && cr[2] >= 0.0f) ||
+                      (cr[0] <= 0.0f && cr[1] <= 0.0f && cr[2] <= 0.0f);
+  const float sd = inside ? best : -best;
+  const float cov = sigmoid_rounded(div_rn_inv(sd, K.sigma_eff, K.inv_sigma));
+  o.cov = deep ? 1.0f : cov;
   o.w = __fmul_rn(r.alpha, o.cov);
-  o.band = !(dist < 1e-9f);
-  if (kGrad && o.band) cov_grad_ref(r, e, t, dist, o.cov, inside, ptx, pty, K, o);
-  return o.w <= kMinWeight ? kSkip : kHit;
+  o.band = !deep && !(best < 1e-9f);
+  if (kGrad) cov_grad_ref(r, edge, bt, best, o.cov, inside, ptx, pty, K, o);
+  return (live && !(o.w <= kMinWeight)) ? kHit : kSkip;
 }
 
 // Running product of (1 - w) with 2^64 renormalisation and barrier tracking.
@@ -816,8 +845,6 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
       const TriRec& r = sm.rec[j];
       const int k = sm.kidx[j];
       const int cand = code >> kCandShift;
-      const bool single = kPrec == kPrecRef && (cand & (cand - 1)) == 0;
-      const int e1 = cand - 1 - (cand >> 2);  // the single candidate: 1, 2, 4 -> 0, 1, 2
 #pragma unroll
       for (int q = 0; q < kPPT; ++q) {
         if (!active[q]) continue;
@@ -826,8 +853,8 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
         if (code & kBlkInside) {
           pe.w = r.alpha;
           st = kHit;
-        } else if (single) {
-          st = eval_single<false>(r, code, e1, px, py[q], ptx, pty[q], K, pe);
+        } else if (kPrec == kPrecRef) {
+          st = eval_cand<false>(r, code, cand, px, py[q], ptx, pty[q], K, pe);
         } else {
           st = eval_pair<false, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
         }
@@ -925,8 +952,8 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
           pe.cov = 1.0f;
           pe.band = false;
           st = kHit;
-        } else if (single) {
-          st = eval_single<true>(r, code, e1, px, py[q], ptx, pty[q], K, pe);
+        } else if (kPrec == kPrecRef) {
+          st = eval_cand<true>(r, code, cand, px, py[q], ptx, pty[q], K, pe);
         } else {
           st = eval_pair<true, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
         }
@@ -956,8 +983,8 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
           const float ax = __fmul_rn(d_cov, pe.dax), ay = __fmul_rn(d_cov, pe.day);
           const float bx = __fmul_rn(d_cov, pe.dbx), by = __fmul_rn(d_cov, pe.dby);
           if (single) {
-            // An exact-path pixel of a single-edge block that composites has
-            // edge e as its nearest edge too (see eval_single).
+            // With one candidate edge e every compositing pixel's nearest
+            // edge is e (eval_cand), the exact path's included.
             acc[0] += ax;
             acc[1] += ay;
             acc[2] += bx;
