@@ -1068,7 +1068,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
 
 __global__ void dr_mse_kernel(const float* __restrict__ img, const float* __restrict__ tgt,
                               long long n, float* __restrict__ losses) {
-  __shared__ double part[kWarps];
+  __shared__ double part[32];  // one per warp of a block of up to 1024 threads
   const float* x = img + (size_t)blockIdx.x * n;
   const float* y = tgt + (size_t)blockIdx.x * n;
   double s = 0.0;
