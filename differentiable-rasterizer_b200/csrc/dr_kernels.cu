@@ -626,6 +626,43 @@ __device__ __forceinline__ int eval_cand(const TriRec& r, int code, int cand, in
   return (live && !(o.w <= kMinWeight)) ? kHit : kSkip;
 }
 
+// eval_cand for a block whose only candidate is edge E, straight-line: the
+// other two cross products have the winding's sign, so is_inside reduces to
+// the sign of edge E's cross product against the winding.
+template <bool kGrad, int E>
+__device__ __forceinline__ int eval_single(const TriRec& r, int code, int px, int py, float ptx,
+                                           float pty, const Consts& K, PairEval& o) {
+  bool live = true;
+  if (code & kBlkBox) {
+    live = (px >= r.bbox[0]) & (px < r.bbox[2]) & (py >= r.bbox[1]) & (py < r.bbox[3]);
+  }
+  const float l = __fmaf_rn(r.n[2 * E], ptx, __fmaf_rn(r.n[2 * E + 1], pty, r.c[E]));
+  live = live && !(l < -r.rej);
+  const bool deep = l > r.acc;
+  const SegEval g = seg_exact(r, E, ptx, pty);
+  const bool inside = r.wind > 0.0f ? g.cross >= 0.0f : g.cross <= 0.0f;
+  const float sd = inside ? g.d : -g.d;
+  const float cov = sigmoid_rounded(div_rn_inv(sd, K.sigma_eff, K.inv_sigma));
+  o.cov = deep ? 1.0f : cov;
+  o.w = __fmul_rn(r.alpha, o.cov);
+  o.band = !deep && !(g.d < 1e-9f);
+  if (kGrad) cov_grad_ref(r, E, g.t, g.d, o.cov, inside, ptx, pty, K, o);
+  return (live && !(o.w <= kMinWeight)) ? kHit : kSkip;
+}
+
+// Reference-precision soft-edge evaluation, dispatched on the (warp-uniform)
+// candidate set.
+template <bool kGrad>
+__device__ __forceinline__ int eval_ref_prec(const TriRec& r, int code, int cand, int px, int py,
+                                             float ptx, float pty, const Consts& K, PairEval& o) {
+  if (r.flags & kFastOk) {
+    if (cand == 1) return eval_single<kGrad, 0>(r, code, px, py, ptx, pty, K, o);
+    if (cand == 2) return eval_single<kGrad, 1>(r, code, px, py, ptx, pty, K, o);
+    if (cand == 4) return eval_single<kGrad, 2>(r, code, px, py, ptx, pty, K, o);
+  }
+  return eval_cand<kGrad>(r, code, cand, px, py, ptx, pty, K, o);
+}
+
 // Running product of (1 - w) with 2^64 renormalisation and barrier tracking.
 struct Prod {
   float m;
@@ -854,7 +891,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
           pe.w = r.alpha;
           st = kHit;
         } else if (kPrec == kPrecRef) {
-          st = eval_cand<false>(r, code, cand, px, py[q], ptx, pty[q], K, pe);
+          st = eval_ref_prec<false>(r, code, cand, px, py[q], ptx, pty[q], K, pe);
         } else {
           st = eval_pair<false, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
         }
@@ -953,7 +990,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
           pe.band = false;
           st = kHit;
         } else if (kPrec == kPrecRef) {
-          st = eval_cand<true>(r, code, cand, px, py[q], ptx, pty[q], K, pe);
+          st = eval_ref_prec<true>(r, code, cand, px, py[q], ptx, pty[q], K, pe);
         } else {
           st = eval_pair<true, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
         }
