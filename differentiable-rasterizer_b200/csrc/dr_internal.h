@@ -18,6 +18,7 @@ struct RasterArgs {
   int B, T, H, W;
   int tiles_x;
   int tile_row0, tile_row_step;  // tile rows covered: row0 + i * step
+  int tile_rows;                 // number of covered tile rows (set by launch_raster)
   float sigma_eff;               // max(sigma, 1e-8) (raster.rs:75)
   float inv_sigma;               // 1 / sigma_eff
   int precision;                 // 0 reference rounding, 1 strict, 2 fast (band arithmetic)

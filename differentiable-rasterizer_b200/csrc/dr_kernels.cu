@@ -28,16 +28,12 @@
 
 namespace dr {
 
-#ifndef DR_PPT
-#define DR_PPT 1
-#endif
 constexpr int kTile = 16;
-constexpr int kPPT = DR_PPT;                             // pixels per thread (1 or 2)
-constexpr int kBlockW = 8, kBlockH = 4 * kPPT;           // one warp's pixel block
+constexpr int kBlockW = 8, kBlockH = 4;                  // one warp's pixel block, a pixel per lane
 constexpr int kWarps = (kTile / kBlockW) * (kTile / kBlockH);
 constexpr int kThreads = kWarps * 32;
-static_assert(kWarps <= 8, "block codes are one byte per warp in one 64-bit word");
 constexpr int kChunk = 128;                              // triangles binned per round (<= kThreads)
+constexpr int kRegionBlocks = 4 * kWarps;                // region kernel: 2 x 2 tiles
 constexpr float kRenorm = 18446744073709551616.0f;        // 2^64
 constexpr float kRenormInv = 5.42101086242752217e-20f;    // 2^-64
 
@@ -205,6 +201,20 @@ struct Smem {
   int is_last;
 };
 
+// Region kernel (a list of at most kChunk triangles): one CTA per 2 x 2
+// tiles, one code per warp block of the region, warps taking blocks from a
+// shared counter.
+struct RegionSmem {
+  TriRec rec[kChunk];
+  unsigned char bcode[kChunk][kRegionBlocks];
+  int kidx[kChunk];
+  float acc[kChunk][kParams];
+  int warp_count[kWarps];
+  double loss_part[kRegionBlocks];
+  int next_block;
+  int is_last;
+};
+
 // Block code of one warp block [bx0,bx1) x [by0,by1) (clipped to the image)
 // for one triangle record.
 __device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0, int bx1, int by1,
@@ -278,6 +288,76 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
     float4* dst = reinterpret_cast<float4*>(&sm.rec[slot]);
 #pragma unroll
     for (int j = 0; j < kRecWords / 4; ++j) dst[j] = src[j];
+  }
+  __syncthreads();
+  return total;
+}
+
+// Pixel origin of warp block `blk` of a region: 4 tiles of 8 blocks in the
+// order left-top, right-top, left-bottom, right-bottom; each tile's blocks as
+// the tile kernel's warps (2 columns x 4 rows). A block on a tile row the
+// launch does not cover gets y0 = H: empty.
+__device__ __forceinline__ void region_block_origin(const RasterArgs& a, int rx0, int lrow0,
+                                                    int blk, int& x0, int& y0) {
+  const int t = blk >> 3, wb = blk & 7;
+  x0 = rx0 + (t & 1) * kTile + (wb & 1) * kBlockW;
+  const int lr = lrow0 + (t >> 1);
+  y0 = lr < a.tile_rows ? (a.tile_row0 + lr * a.tile_row_step) * kTile + (wb >> 1) * kBlockH
+                        : a.H;
+}
+
+// The region's whole list (a.T <= kChunk), in order: two threads per
+// triangle, each classifying 16 of the 32 blocks. Also clears the gradient
+// accumulators.
+__device__ int build_region_list(RegionSmem& sm, const RasterArgs& a,
+                                 const TriRec* __restrict__ recs, int rx0, int lrow0) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int half = threadIdx.x & 1;
+  const int k = (int)threadIdx.x >> 1;
+  constexpr int kPer = kRegionBlocks / 2;
+  static_assert(kPer == 16 && kThreads / 2 == kChunk, "two threads per triangle, 16 blocks each");
+  bool keep_half = false;
+  unsigned long long lo = 0x0101010101010101ull, hi = lo;  // all kBlkSkip
+  const TriRec* r = recs + k;
+  if (k < a.T && (r->flags & kLive)) {
+    lo = hi = 0;
+#pragma unroll 1
+    for (int i = 0; i < kPer; ++i) {
+      int x0, y0;
+      region_block_origin(a, rx0, lrow0, half * kPer + i, x0, y0);
+      const int c =
+          classify_block(*r, x0, y0, min(x0 + kBlockW, a.W), min(y0 + kBlockH, a.H), a.W, a.H);
+      keep_half |= !(c & kBlkSkip);
+      if (i < 8) lo |= (unsigned long long)c << (8 * i);
+      else hi |= (unsigned long long)c << (8 * (i - 8));
+    }
+  }
+  // Every lane must take part in the shuffle: it may not sit behind `||`.
+  const bool partner_keeps = __shfl_xor_sync(0xffffffffu, keep_half, 1);
+  const bool keep = keep_half || partner_keeps;
+  const unsigned ballot = __ballot_sync(0xffffffffu, keep && !half);  // one bit per triangle
+  if (lane == 0) sm.warp_count[warp] = __popc(ballot);
+  for (int i = threadIdx.x; i < kChunk * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
+  __syncthreads();
+  int base = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const int cnt = sm.warp_count[w];
+    base += (w < warp) ? cnt : 0;
+    total += cnt;
+  }
+  if (keep) {
+    const int slot = base + __popc(ballot & ((1u << (lane & ~1)) - 1u));
+    unsigned long long* dst_code = reinterpret_cast<unsigned long long*>(&sm.bcode[slot][half * kPer]);
+    dst_code[0] = lo;
+    dst_code[1] = hi;
+    if (!half) {
+      sm.kidx[slot] = k;
+      const float4* src = reinterpret_cast<const float4*>(r);
+      float4* dst = reinterpret_cast<float4*>(&sm.rec[slot]);
+#pragma unroll
+      for (int j = 0; j < kRecWords / 4; ++j) dst[j] = src[j];
+    }
   }
   __syncthreads();
   return total;
@@ -825,6 +905,236 @@ __device__ __forceinline__ size_t pix_index(int layout, int b, int ch, int px, i
   return (((size_t)b * H + py) * W + px) * 3 + ch;
 }
 
+// Pass 1 over a staged list for one lane's pixel: composites in order
+// (raster.rs:63) and keeps the running product of 1 - w. `col` selects the
+// warp's block code.
+template <int Mode, int kPrec, class S>
+__device__ __forceinline__ void forward_walk(const S& sm, int count, int col, int px, int py,
+                                             float ptx, float pty, bool active, const Consts& K,
+                                             float& c0, float& c1, float& c2, Prod& P) {
+  for (int j = 0; j < count; ++j) {
+    const int code = sm.bcode[j][col];
+    if (code & kBlkSkip) continue;
+    const TriRec& r = sm.rec[j];
+    const int k = sm.kidx[j];
+    const int cand = code >> kCandShift;
+    PairEval pe;
+    int st;
+    if (code & kBlkInside) {
+      pe.w = r.alpha;
+      st = kHit;
+    } else if (kPrec == kPrecRef) {
+      st = eval_ref_prec<false>(r, code, cand, px, py, ptx, pty, K, pe);
+    } else {
+      st = eval_pair<false, kPrec>(r, code, px, py, ptx, pty, K, pe);
+    }
+    if (st == kExact) {
+      pe = eval_ref<false>(&r, ptx, pty, K.sigma_eff);
+      st = pe.hit ? kHit : kSkip;
+    }
+    if (st != kHit || !active) continue;
+    const float w = pe.w, om = __fsub_rn(1.0f, w);
+    c0 = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(c0, om));  // raster.rs:63
+    c1 = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(c1, om));
+    c2 = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(c2, om));
+    if (Mode != kModeRender) P.mul(om, k);
+  }
+}
+
+// Pass 2 over a staged list: recomposites in forward order, and per entry
+// reduces the warp's contributions into sm.acc (one shared atomic per value).
+template <int kPrec, class S>
+__device__ __forceinline__ void gradient_walk(S& sm, int count, int col, int lane, int px, int py,
+                                              float ptx, float pty, bool active, const Consts& K,
+                                              const Prod& P, Prod& Q, float G0, float G1,
+                                              float G2, float& r0, float& r1, float& r2) {
+  const int slot10 = reduce10_slot(lane);
+  for (int j = 0; j < count; ++j) {
+    const int code = sm.bcode[j][col];
+    if (code & kBlkSkip) continue;
+    const TriRec& r = sm.rec[j];
+    const int k = sm.kidx[j];
+    const int cand = code >> kCandShift;
+    // Single-edge entries accumulate vertex gradients relative to the edge
+    // (acc[0..3] = vertex e, vertex e + 1), others by vertex (acc[0..5]).
+    const bool single = kPrec == kPrecRef && !(code & kBlkInside) && (cand & (cand - 1)) == 0;
+    const int e1 = cand - 1 - (cand >> 2);  // the single candidate: 1, 2, 4 -> 0, 1, 2
+    float acc[10];
+#pragma unroll
+    for (int i = 0; i < 10; ++i) acc[i] = 0.0f;
+    bool contrib = false, band = false;
+    PairEval pe;
+    int st;
+    if (code & kBlkInside) {
+      pe.w = r.alpha;
+      pe.cov = 1.0f;
+      pe.band = false;
+      st = kHit;
+    } else if (kPrec == kPrecRef) {
+      st = eval_ref_prec<true>(r, code, cand, px, py, ptx, pty, K, pe);
+    } else {
+      st = eval_pair<true, kPrec>(r, code, px, py, ptx, pty, K, pe);
+    }
+    if (st == kExact) {
+      pe = eval_ref<true>(&r, ptx, pty, K.sigma_eff);
+      st = pe.hit ? kHit : kSkip;
+    }
+    if (st == kHit && active) {
+      contrib = true;
+      const float w = pe.w, om = __fsub_rn(1.0f, w);
+      Q.mul(om, k);
+      const float A = attenuation(P, Q, k);
+      const float g0 = __fmul_rn(G0, A), g1 = __fmul_rn(G1, A), g2 = __fmul_rn(G2, A);
+      // grad.rs:162-179
+      acc[6] = __fmul_rn(g0, w);
+      acc[7] = __fmul_rn(g1, w);
+      acc[8] = __fmul_rn(g2, w);
+      float d_w = __fmul_rn(g0, __fsub_rn(r.color[0], r0));
+      d_w = __fmaf_rn(g1, __fsub_rn(r.color[1], r1), d_w);
+      d_w = __fmaf_rn(g2, __fsub_rn(r.color[2], r2), d_w);
+      if (r.flags & kAlphaActive) acc[9] = __fmul_rn(d_w, pe.cov);
+      // coverage_with_grad (grad.rs:231-270): nonzero only for band pairs
+      // away from the boundary itself (dist >= 1e-9).
+      if (pe.band) {
+        band = true;
+        const float d_cov = __fmul_rn(d_w, r.alpha);
+        const float ax = __fmul_rn(d_cov, pe.dax), ay = __fmul_rn(d_cov, pe.day);
+        const float bx = __fmul_rn(d_cov, pe.dbx), by = __fmul_rn(d_cov, pe.dby);
+        if (single) {
+          // With one candidate edge e every compositing pixel's nearest
+          // edge is e (eval_cand).
+          acc[0] = ax;
+          acc[1] = ay;
+          acc[2] = bx;
+          acc[3] = by;
+        } else {
+          const int e = pe.edge;
+          acc[0] = (e == 0) ? ax : ((e == 2) ? bx : 0.0f);
+          acc[1] = (e == 0) ? ay : ((e == 2) ? by : 0.0f);
+          acc[2] = (e == 1) ? ax : ((e == 0) ? bx : 0.0f);
+          acc[3] = (e == 1) ? ay : ((e == 0) ? by : 0.0f);
+          acc[4] = (e == 2) ? ax : ((e == 1) ? bx : 0.0f);
+          acc[5] = (e == 2) ? ay : ((e == 1) ? by : 0.0f);
+        }
+      }
+      r0 = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(r0, om));  // raster.rs:63
+      r1 = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(r1, om));
+      r2 = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(r2, om));
+    }
+    // Per warp: one transposed reduction, then one shared atomic per value.
+    const unsigned any = __ballot_sync(0xffffffffu, contrib);
+    if (any == 0u) continue;
+    if (__any_sync(0xffffffffu, band)) {
+      if (single) {
+        const float v8[8] = {acc[0], acc[1], acc[2], acc[3], acc[6], acc[7], acc[8], acc[9]};
+        const float sum = reduce8(v8, lane);
+        const int prm = reduce8_param(lane, e1);
+        if (prm >= 0) atomicAdd(&sm.acc[j][prm], sum);
+      } else {
+        const float sum = reduce10(acc, lane);
+        if (slot10 >= 0) atomicAdd(&sm.acc[j][slot10], sum);
+      }
+    } else {
+      const float sum = reduce4(acc[6], acc[7], acc[8], acc[9], lane);
+      if ((lane & 7) == 0) atomicAdd(&sm.acc[j][6 + (lane >> 3)], sum);
+    }
+  }
+}
+
+// The canvas a scene starts from: one shared colour or one per scene.
+__device__ __forceinline__ void scene_background(const RasterArgs& a, int b, float& c0, float& c1,
+                                                 float& c2) {
+  c0 = a.bg3[0];
+  c1 = a.bg3[1];
+  c2 = a.bg3[2];
+  if (a.bg_dev) {
+    const float* q = a.bg_dev + (a.bg_per_scene ? 3 * b : 0);
+    c0 = q[0];
+    c1 = q[1];
+    c2 = q[2];
+  }
+}
+
+// G = (2/N)(r - t) (grad.rs:112-114) or the upstream gradient, and the pixel's
+// squared error for the loss.
+template <int Mode>
+__device__ __forceinline__ void top_gradient(const RasterArgs& a, int b, int px, int py,
+                                             bool active, float c0, float c1, float c2, float& G0,
+                                             float& G1, float& G2, double& sq) {
+  G0 = G1 = G2 = 0.0f;
+  sq = 0.0;
+  if (!active) return;
+  const float o0 = a.other[pix_index(a.layout, b, 0, px, py, a.W, a.H)];
+  const float o1 = a.other[pix_index(a.layout, b, 1, px, py, a.W, a.H)];
+  const float o2 = a.other[pix_index(a.layout, b, 2, px, py, a.W, a.H)];
+  if (Mode == kModeLoss) {
+    const float d0 = __fsub_rn(c0, o0), d1 = __fsub_rn(c1, o1), d2 = __fsub_rn(c2, o2);
+    sq = (double)d0 * d0 + (double)d1 * d1 + (double)d2 * d2;
+    G0 = __fmul_rn(a.grad_scale, d0);
+    G1 = __fmul_rn(a.grad_scale, d1);
+    G2 = __fmul_rn(a.grad_scale, d2);
+  } else {
+    G0 = o0;
+    G1 = o1;
+    G2 = o2;
+  }
+}
+
+__device__ __forceinline__ void store_pixel(const RasterArgs& a, int b, int px, int py, float c0,
+                                            float c1, float c2) {
+  a.image[pix_index(a.layout, b, 0, px, py, a.W, a.H)] = c0;
+  a.image[pix_index(a.layout, b, 1, px, py, a.W, a.H)] = c1;
+  a.image[pix_index(a.layout, b, 2, px, py, a.W, a.H)] = c2;
+}
+
+// One global atomic per nonzero (triangle, parameter) accumulator of a list.
+template <class S>
+__device__ __forceinline__ void flush_grads(const S& sm, const RasterArgs& a, int b, int count) {
+  float* g = a.grads + (size_t)b * a.T * kParams;
+  for (int i = threadIdx.x; i < count * kParams; i += kThreads) {
+    const float v = (&sm.acc[0][0])[i];
+    if (v != 0.0f) atomicAdd(&g[(size_t)sm.kidx[i / kParams] * kParams + (i % kParams)], v);
+  }
+}
+
+// Per-scene loss: each CTA's f64 partial (slot `slot` of the scene's n_blocks),
+// summed in fixed order by the scene's last CTA (canvas.rs:45-59). `part`
+// holds this CTA's n_part partials in shared memory; all threads call it after
+// the partials are written.
+__device__ __forceinline__ void scene_loss(const RasterArgs& a, int b, int slot, int n_blocks,
+                                           const double* part, int n_part, double* sm_scratch,
+                                           int* is_last) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int w = 0; w < n_part; ++w) s += part[w];
+    a.loss_partials[(size_t)b * n_blocks + slot] = s;
+    __threadfence();
+    const unsigned prev = atomicAdd(&a.loss_counters[b], 1u);
+    *is_last = (prev == (unsigned)(n_blocks - 1));
+  }
+  __syncthreads();
+  if (*is_last) {
+    __threadfence();
+    double s = 0.0;
+    for (int t = threadIdx.x; t < n_blocks; t += kThreads)
+      s += *((volatile double*)&a.loss_partials[(size_t)b * n_blocks + t]);
+    s = warp_sum_d(s);
+    if (lane == 0) sm_scratch[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double tot = 0.0;
+      for (int w = 0; w < kWarps; ++w) tot += sm_scratch[w];
+      if (a.loss_sums) a.loss_sums[b] = tot;
+      if (a.losses) a.losses[b] = (float)(tot / a.n_values);  // canvas.rs:58
+      a.loss_counters[b] = 0;
+    }
+  }
+}
+
+// Tile kernel: one CTA per (scene, 16x16 tile), warp w on block w; lists
+// longer than kChunk are binned in chunks behind barriers.
 template <int Mode, int kPrec>
 __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -836,128 +1146,44 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   const int tile_col = local_tile % a.tiles_x;
   const int tile_row = a.tile_row0 + (local_tile / a.tiles_x) * a.tile_row_step;
   const int tx0 = tile_col * kTile, ty0 = tile_row * kTile;
-
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int px = tx0 + (warp & 1) * kBlockW + (lane & 7);
-  int py[kPPT];
-  bool active[kPPT];
-  float pty[kPPT];
-#pragma unroll
-  for (int q = 0; q < kPPT; ++q) {
-    py[q] = ty0 + (warp >> 1) * kBlockH + (lane >> 3) + 4 * q;
-    active[q] = px < a.W && py[q] < a.H;
-    pty[q] = pixel_center(py[q], a.H);
-  }
-  const float ptx = pixel_center(px, a.W);
-
+  const int py = ty0 + (warp >> 1) * kBlockH + (lane >> 3);
+  const bool active = px < a.W && py < a.H;
+  const float ptx = pixel_center(px, a.W), pty = pixel_center(py, a.H);
   const TriRec* recs = a.recs + (size_t)b * a.T;
-  float bg0 = a.bg3[0], bg1 = a.bg3[1], bg2 = a.bg3[2];
-  if (a.bg_dev) {
-    const float* q = a.bg_dev + (a.bg_per_scene ? 3 * b : 0);
-    bg0 = q[0];
-    bg1 = q[1];
-    bg2 = q[2];
-  }
   Consts K;
   K.sigma_eff = a.sigma_eff;
   K.inv_sigma = a.inv_sigma;
   const int n_chunks = (a.T + kChunk - 1) / kChunk;
 
   // ---- pass 1: forward composite ------------------------------------------
-  float c0[kPPT], c1[kPPT], c2[kPPT];
-  Prod P[kPPT];
-#pragma unroll
-  for (int q = 0; q < kPPT; ++q) {
-    c0[q] = bg0;
-    c1[q] = bg1;
-    c2[q] = bg2;
-    P[q].init();
-  }
+  float c0, c1, c2;
+  scene_background(a, b, c0, c1, c2);
+  Prod P;
+  P.init();
   int count = 0;
   for (int ci = 0; ci < n_chunks; ++ci) {
     count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H);
-    for (int j = 0; j < count; ++j) {
-      const int code = sm.bcode[j][warp];
-      if (code & kBlkSkip) continue;
-      const TriRec& r = sm.rec[j];
-      const int k = sm.kidx[j];
-      const int cand = code >> kCandShift;
-#pragma unroll
-      for (int q = 0; q < kPPT; ++q) {
-        if (!active[q]) continue;
-        PairEval pe;
-        int st;
-        if (code & kBlkInside) {
-          pe.w = r.alpha;
-          st = kHit;
-        } else if (kPrec == kPrecRef) {
-          st = eval_ref_prec<false>(r, code, cand, px, py[q], ptx, pty[q], K, pe);
-        } else {
-          st = eval_pair<false, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
-        }
-        if (st == kExact) {
-          pe = eval_ref<false>(&r, ptx, pty[q], K.sigma_eff);
-          st = pe.hit ? kHit : kSkip;
-        }
-        if (st == kSkip) continue;
-        const float w = pe.w, om = __fsub_rn(1.0f, w);
-        c0[q] = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(c0[q], om));  // raster.rs:63
-        c1[q] = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(c1[q], om));
-        c2[q] = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(c2[q], om));
-        if (Mode != kModeRender) P[q].mul(om, k);
-      }
-    }
+    forward_walk<Mode, kPrec>(sm, count, warp, px, py, ptx, pty, active, K, c0, c1, c2, P);
   }
-
-  if (a.image) {
-#pragma unroll
-    for (int q = 0; q < kPPT; ++q) {
-      if (!active[q]) continue;
-      a.image[pix_index(a.layout, b, 0, px, py[q], a.W, a.H)] = c0[q];
-      a.image[pix_index(a.layout, b, 1, px, py[q], a.W, a.H)] = c1[q];
-      a.image[pix_index(a.layout, b, 2, px, py[q], a.W, a.H)] = c2[q];
-    }
-  }
+  if (a.image && active) store_pixel(a, b, px, py, c0, c1, c2);
   if (Mode == kModeRender) return;
 
   // ---- loss and the gradient reaching the top of the stack ----------------
-  float G0[kPPT], G1[kPPT], G2[kPPT];
-  double sq = 0.0;
-#pragma unroll
-  for (int q = 0; q < kPPT; ++q) {
-    G0[q] = G1[q] = G2[q] = 0.0f;
-    if (!active[q]) continue;
-    const float o0 = a.other[pix_index(a.layout, b, 0, px, py[q], a.W, a.H)];
-    const float o1 = a.other[pix_index(a.layout, b, 1, px, py[q], a.W, a.H)];
-    const float o2 = a.other[pix_index(a.layout, b, 2, px, py[q], a.W, a.H)];
-    if (Mode == kModeLoss) {
-      const float d0 = __fsub_rn(c0[q], o0), d1 = __fsub_rn(c1[q], o1), d2 = __fsub_rn(c2[q], o2);
-      sq += (double)d0 * d0 + (double)d1 * d1 + (double)d2 * d2;
-      G0[q] = __fmul_rn(a.grad_scale, d0);  // grad.rs:112-114
-      G1[q] = __fmul_rn(a.grad_scale, d1);
-      G2[q] = __fmul_rn(a.grad_scale, d2);
-    } else {
-      G0[q] = o0;
-      G1[q] = o1;
-      G2[q] = o2;
-    }
-  }
+  float G0, G1, G2;
+  double sq;
+  top_gradient<Mode>(a, b, px, py, active, c0, c1, c2, G0, G1, G2, sq);
   if (Mode == kModeLoss) {
     const double ws = warp_sum_d(sq);
     if (lane == 0) sm.loss_part[warp] = ws;
   }
 
   // ---- pass 2: recomposite in forward order and accumulate gradients ------
-  const int slot10 = reduce10_slot(lane);
-  float r0[kPPT], r1[kPPT], r2[kPPT];
-  Prod Q[kPPT];
-#pragma unroll
-  for (int q = 0; q < kPPT; ++q) {
-    r0[q] = bg0;
-    r1[q] = bg1;
-    r2[q] = bg2;
-    Q[q].init();
-  }
+  float r0, r1, r2;
+  scene_background(a, b, r0, r1, r2);
+  Prod Q;
+  Q.init();
   for (int ci = 0; ci < n_chunks; ++ci) {
     if (n_chunks > 1) {
       __syncthreads();
@@ -965,138 +1191,95 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     }
     for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
     __syncthreads();
-    for (int j = 0; j < count; ++j) {
-      const int code = sm.bcode[j][warp];
-      if (code & kBlkSkip) continue;
-      const TriRec& r = sm.rec[j];
-      const int k = sm.kidx[j];
-      const int cand = code >> kCandShift;
-      // Single-edge entries accumulate vertex gradients relative to the edge
-      // (acc[0..3] = vertex e, vertex e + 1), others by vertex (acc[0..5]).
-      const bool single = kPrec == kPrecRef && !(code & kBlkInside) && (cand & (cand - 1)) == 0;
-      const int e1 = cand - 1 - (cand >> 2);
-      float acc[10];
-#pragma unroll
-      for (int i = 0; i < 10; ++i) acc[i] = 0.0f;
-      bool contrib = false, band = false;
-#pragma unroll
-      for (int q = 0; q < kPPT; ++q) {
-        if (!active[q]) continue;
-        PairEval pe;
-        int st;
-        if (code & kBlkInside) {
-          pe.w = r.alpha;
-          pe.cov = 1.0f;
-          pe.band = false;
-          st = kHit;
-        } else if (kPrec == kPrecRef) {
-          st = eval_ref_prec<true>(r, code, cand, px, py[q], ptx, pty[q], K, pe);
-        } else {
-          st = eval_pair<true, kPrec>(r, code, px, py[q], ptx, pty[q], K, pe);
-        }
-        if (st == kExact) {
-          pe = eval_ref<true>(&r, ptx, pty[q], K.sigma_eff);
-          st = pe.hit ? kHit : kSkip;
-        }
-        if (st == kSkip) continue;
-        contrib = true;
-        const float w = pe.w, om = __fsub_rn(1.0f, w);
-        Q[q].mul(om, k);
-        const float A = attenuation(P[q], Q[q], k);
-        const float g0 = __fmul_rn(G0[q], A), g1 = __fmul_rn(G1[q], A), g2 = __fmul_rn(G2[q], A);
-        // grad.rs:162-179
-        acc[6] = __fmaf_rn(g0, w, acc[6]);
-        acc[7] = __fmaf_rn(g1, w, acc[7]);
-        acc[8] = __fmaf_rn(g2, w, acc[8]);
-        float d_w = __fmul_rn(g0, __fsub_rn(r.color[0], r0[q]));
-        d_w = __fmaf_rn(g1, __fsub_rn(r.color[1], r1[q]), d_w);
-        d_w = __fmaf_rn(g2, __fsub_rn(r.color[2], r2[q]), d_w);
-        if (r.flags & kAlphaActive) acc[9] = __fmaf_rn(d_w, pe.cov, acc[9]);
-        // coverage_with_grad (grad.rs:231-270): nonzero only for band pairs
-        // away from the boundary itself (dist >= 1e-9).
-        if (pe.band) {
-          band = true;
-          const float d_cov = __fmul_rn(d_w, r.alpha);
-          const float ax = __fmul_rn(d_cov, pe.dax), ay = __fmul_rn(d_cov, pe.day);
-          const float bx = __fmul_rn(d_cov, pe.dbx), by = __fmul_rn(d_cov, pe.dby);
-          if (single) {
-            // With one candidate edge e every compositing pixel's nearest
-            // edge is e (eval_cand), the exact path's included.
-            acc[0] += ax;
-            acc[1] += ay;
-            acc[2] += bx;
-            acc[3] += by;
-          } else {
-            const int e = pe.edge;
-            acc[0] += (e == 0) ? ax : ((e == 2) ? bx : 0.0f);
-            acc[1] += (e == 0) ? ay : ((e == 2) ? by : 0.0f);
-            acc[2] += (e == 1) ? ax : ((e == 0) ? bx : 0.0f);
-            acc[3] += (e == 1) ? ay : ((e == 0) ? by : 0.0f);
-            acc[4] += (e == 2) ? ax : ((e == 1) ? bx : 0.0f);
-            acc[5] += (e == 2) ? ay : ((e == 1) ? by : 0.0f);
-          }
-        }
-        r0[q] = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(r0[q], om));  // raster.rs:63
-        r1[q] = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(r1[q], om));
-        r2[q] = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(r2[q], om));
-      }
-      // Per warp: one transposed reduction, then one shared atomic per value.
-      const unsigned any = __ballot_sync(0xffffffffu, contrib);
-      if (any == 0u) continue;
-      if (__any_sync(0xffffffffu, band)) {
-        if (single) {
-          const float v8[8] = {acc[0], acc[1], acc[2], acc[3], acc[6], acc[7], acc[8], acc[9]};
-          const float s = reduce8(v8, lane);
-          const int prm = reduce8_param(lane, e1);
-          if (prm >= 0) atomicAdd(&sm.acc[j][prm], s);
-        } else {
-          const float s = reduce10(acc, lane);
-          if (slot10 >= 0) atomicAdd(&sm.acc[j][slot10], s);
-        }
-      } else {
-        const float s = reduce4(acc[6], acc[7], acc[8], acc[9], lane);
-        if ((lane & 7) == 0) atomicAdd(&sm.acc[j][6 + (lane >> 3)], s);
-      }
-    }
+    gradient_walk<kPrec>(sm, count, warp, lane, px, py, ptx, pty, active, K, P, Q, G0, G1, G2, r0,
+                         r1, r2);
     __syncthreads();
-    // One global atomic per (triangle, parameter) per block.
-    float* g = a.grads + (size_t)b * a.T * kParams;
-    for (int i = threadIdx.x; i < count * kParams; i += kThreads) {
-      const float v = (&sm.acc[0][0])[i];
-      if (v != 0.0f) atomicAdd(&g[(size_t)sm.kidx[i / kParams] * kParams + (i % kParams)], v);
-    }
+    flush_grads(sm, a, b, count);
   }
 
-  // ---- per-scene loss: tile partials, summed by the last block ------------
-  if (Mode == kModeLoss) {
-    __syncthreads();
-    const int n_tiles = gridDim.x;
-    if (threadIdx.x == 0) {
-      double s = 0.0;
-      for (int w = 0; w < kWarps; ++w) s += sm.loss_part[w];
-      a.loss_partials[(size_t)b * n_tiles + local_tile] = s;
-      __threadfence();
-      const unsigned prev = atomicAdd(&a.loss_counters[b], 1u);
-      sm.is_last = (prev == (unsigned)(n_tiles - 1));
-    }
-    __syncthreads();
-    if (sm.is_last) {
-      __threadfence();
-      double s = 0.0;
-      for (int t = threadIdx.x; t < n_tiles; t += kThreads)
-        s += *((volatile double*)&a.loss_partials[(size_t)b * n_tiles + t]);
-      s = warp_sum_d(s);
-      if (lane == 0) sm.loss_part[warp] = s;
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        double tot = 0.0;
-        for (int w = 0; w < kWarps; ++w) tot += sm.loss_part[w];
-        if (a.loss_sums) a.loss_sums[b] = tot;
-        if (a.losses) a.losses[b] = (float)(tot / a.n_values);  // canvas.rs:58
-        a.loss_counters[b] = 0;
+  if (Mode == kModeLoss)
+    scene_loss(a, b, blockIdx.x, gridDim.x, sm.loss_part, kWarps, sm.loss_part, &sm.is_last);
+}
+
+// k-th index of 0..n-1 in centre-out order: c, c-1, c+1, c-2, c+2, ...
+__device__ __forceinline__ int center_out(int k, int n) {
+  const int c = (n - 1) >> 1, j = (k + 1) >> 1;
+  const int idx = (k & 1) ? c - j : c + j;
+  return idx < 0 ? c + j : idx;
+}
+
+// Region kernel, for scenes whose whole list fits one chunk (T <= kChunk):
+// one CTA per (scene, 2 x 2 tiles), the list binned once for all 32 warp
+// blocks, warps taking blocks from a shared counter. A warp that finishes a
+// cheap block takes the next one instead of waiting for the CTA's busiest
+// warp; there is no barrier between the list and the final flush.
+template <int Mode, int kPrec>
+__global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  RegionSmem& sm = *reinterpret_cast<RegionSmem*>(smem_raw);
+  if (a.skip_flag && *a.skip_flag) return;
+
+  // 1-D grid over (region, scene), scenes fastest and regions centre-out:
+  // central regions carry the most overlapping geometry, and the light edge
+  // regions then fill the tail of the launch.
+  const int regions_x = (a.tiles_x + 1) >> 1, regions_y = (a.tile_rows + 1) >> 1;
+  const int n_regions = regions_x * regions_y;
+  const int b = (int)(blockIdx.x % (unsigned)a.B);
+  const int rank = (int)(blockIdx.x / (unsigned)a.B);
+  const int rx = center_out(rank % regions_x, regions_x);
+  const int ry = center_out(rank / regions_x, regions_y);
+  const int region = ry * regions_x + rx;
+  const int rx0 = rx * 2 * kTile;
+  const int lrow0 = ry * 2;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  Consts K;
+  K.sigma_eff = a.sigma_eff;
+  K.inv_sigma = a.inv_sigma;
+
+  if (threadIdx.x == 0) sm.next_block = kWarps;
+  const int count = build_region_list(sm, a, a.recs + (size_t)b * a.T, rx0, lrow0);
+
+  // Blocks are taken at most once each, so no warp runs more than
+  // kRegionBlocks iterations.
+  int blk = warp;
+  for (int it = 0; it < kRegionBlocks; ++it) {
+    int x0, y0;
+    region_block_origin(a, rx0, lrow0, blk, x0, y0);
+    const int px = x0 + (lane & 7), py = y0 + (lane >> 3);
+    const bool active = px < a.W && py < a.H;
+    const float ptx = pixel_center(px, a.W), pty = pixel_center(py, a.H);
+    float c0, c1, c2;
+    scene_background(a, b, c0, c1, c2);
+    Prod P;
+    P.init();
+    forward_walk<Mode, kPrec>(sm, count, blk, px, py, ptx, pty, active, K, c0, c1, c2, P);
+    if (a.image && active) store_pixel(a, b, px, py, c0, c1, c2);
+    if (Mode != kModeRender) {
+      float G0, G1, G2;
+      double sq;
+      top_gradient<Mode>(a, b, px, py, active, c0, c1, c2, G0, G1, G2, sq);
+      if (Mode == kModeLoss) {
+        const double ws = warp_sum_d(sq);
+        if (lane == 0) sm.loss_part[blk] = ws;
       }
+      float r0, r1, r2;
+      scene_background(a, b, r0, r1, r2);
+      Prod Q;
+      Q.init();
+      gradient_walk<kPrec>(sm, count, blk, lane, px, py, ptx, pty, active, K, P, Q, G0, G1, G2,
+                           r0, r1, r2);
     }
+    int next = 0;
+    if (lane == 0) next = atomicAdd(&sm.next_block, 1);
+    blk = __shfl_sync(0xffffffffu, next, 0);
+    if (blk >= kRegionBlocks) break;
   }
+
+  if (Mode == kModeRender) return;
+  __syncthreads();
+  flush_grads(sm, a, b, count);
+  if (Mode == kModeLoss)
+    scene_loss(a, b, region, n_regions, sm.loss_part, kRegionBlocks, sm.loss_part, &sm.is_last);
 }
 
 // ---------------------------------------------------------------------------
@@ -1229,8 +1412,18 @@ cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
 
 static_assert(sizeof(Smem) <= 48 * 1024, "raster smem must fit the default 48 KB limit");
 
+static_assert(sizeof(RegionSmem) <= 48 * 1024, "region smem must fit the default 48 KB limit");
+
+// T <= kChunk: the region kernel (one list per 2 x 2 tiles); otherwise the
+// tile kernel with chunked lists.
 template <int Mode, int kPrec>
 static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
+  if (a.T <= kChunk) {
+    const long long n_ctas = (long long)((a.tiles_x + 1) / 2) * ((a.tile_rows + 1) / 2) * a.B;
+    if (n_ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    dr_raster_region_kernel<Mode, kPrec><<<(unsigned)n_ctas, kThreads, sizeof(RegionSmem), s>>>(a);
+    return cudaGetLastError();
+  }
   dim3 grid(n_tiles, a.B);
   dr_raster_kernel<Mode, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
   return cudaGetLastError();
@@ -1246,8 +1439,13 @@ static cudaError_t launch_prec(int mode, const RasterArgs& a, int n_tiles, cudaS
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s) {
-  if (a.B == 0 || n_tiles == 0) return cudaSuccess;
+// n_tiles: the 16x16 tiles per scene the launch covers (a.tiles_x per covered
+// tile row). Either kernel uses at most n_tiles loss partials per scene.
+cudaError_t launch_raster(int mode, const RasterArgs& args, int n_tiles, cudaStream_t s) {
+  if (args.B == 0 || n_tiles == 0) return cudaSuccess;
+  if (args.tiles_x <= 0) return cudaErrorInvalidValue;
+  RasterArgs a = args;
+  a.tile_rows = n_tiles / a.tiles_x;
   switch (a.precision) {
     case kPrecRef: return launch_prec<kPrecRef>(mode, a, n_tiles, s);
     case kPrecStrict: return launch_prec<kPrecStrict>(mode, a, n_tiles, s);

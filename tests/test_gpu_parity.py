@@ -132,7 +132,9 @@ def test_layouts_agree(native):
     lb, gb = native.loss_backward(p, tgt.permute(0, 3, 1, 2).contiguous(), 0.01,
                                   layout=native.LAYOUT_BCHW)
     assert torch.equal(la, lb)
-    torch.testing.assert_close(ga, gb, rtol=1e-5, atol=1e-9)
+    # Images and losses are bit-identical; gradients are sums of f32 atomics
+    # whose order varies run to run (a few ulps of the largest term).
+    torch.testing.assert_close(ga, gb, rtol=1e-5, atol=1e-8)
 
 
 def test_many_triangles_span_several_bins(native, oracle):
@@ -250,7 +252,8 @@ def test_headline_batch_properties(native):
         lb, gb, ib = native.loss_backward(P[b:b + 1], tgt[b:b + 1], 0.0015, want_image=True)
         assert torch.equal(ib[0], img[b])
         assert lb[0].item() == losses[b].item()
-        torch.testing.assert_close(gb[0], grads[b], rtol=1e-5, atol=1e-9)
+        # f32 atomic accumulation order varies run to run: a few ulps.
+        torch.testing.assert_close(gb[0], grads[b], rtol=1e-5, atol=1e-8)
     mse = ((img.double() - tgt.double()) ** 2).flatten(1).mean(1)
     torch.testing.assert_close(losses.double(), mse, rtol=1e-6, atol=0)
     assert torch.isfinite(grads).all()

@@ -265,4 +265,4 @@ def test_config3_torch_op_path(tl, oracle):
                           targets[32 * r:32 * (r + 1)]) * (32 / 256)
         loss.backward()
         total[32 * r:32 * (r + 1)] = pr.grad
-    torch.testing.assert_close(total, params.grad, rtol=1e-4, atol=1e-9)
+    torch.testing.assert_close(total, params.grad, rtol=1e-4, atol=1e-8)  # atomic order
