@@ -989,9 +989,11 @@ __device__ __forceinline__ void gradient_walk(S& sm, int count, int col, int lan
       acc[6] = __fmul_rn(g0, w);
       acc[7] = __fmul_rn(g1, w);
       acc[8] = __fmul_rn(g2, w);
-      float d_w = __fmul_rn(g0, __fsub_rn(r.color[0], r0));
-      d_w = __fmaf_rn(g1, __fsub_rn(r.color[1], r1), d_w);
-      d_w = __fmaf_rn(g2, __fsub_rn(r.color[2], r2), d_w);
+      const float e0 = __fsub_rn(r.color[0], r0), e1c = __fsub_rn(r.color[1], r1),
+                  e2 = __fsub_rn(r.color[2], r2);
+      float d_w = __fmul_rn(g0, e0);
+      d_w = __fmaf_rn(g1, e1c, d_w);
+      d_w = __fmaf_rn(g2, e2, d_w);
       if (r.flags & kAlphaActive) acc[9] = __fmul_rn(d_w, pe.cov);
       // coverage_with_grad (grad.rs:231-270): nonzero only for band pairs
       // away from the boundary itself (dist >= 1e-9).
@@ -1017,9 +1019,12 @@ __device__ __forceinline__ void gradient_walk(S& sm, int count, int col, int lan
           acc[5] = (e == 2) ? ay : ((e == 1) ? by : 0.0f);
         }
       }
-      r0 = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(r0, om));  // raster.rs:63
-      r1 = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(r1, om));
-      r2 = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(r2, om));
+      // The canvas beneath the next layer. It only feeds d_w, so it is kept
+      // as dst + w (C - dst), within a few ulps of the reference's
+      // C w + dst (1 - w) (raster.rs:63), reusing the differences above.
+      r0 = __fmaf_rn(w, e0, r0);
+      r1 = __fmaf_rn(w, e1c, r1);
+      r2 = __fmaf_rn(w, e2, r2);
     }
     // Per warp: one transposed reduction, then one shared atomic per value.
     const unsigned any = __ballot_sync(0xffffffffu, contrib);
