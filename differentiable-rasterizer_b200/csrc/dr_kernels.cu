@@ -20,6 +20,7 @@
 // Every per-layer gradient term is then available in the same pass that
 // recomposites the canvas, so no tape and no O(T^2) re-walk is needed.
 
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 
@@ -1419,12 +1420,33 @@ static_assert(sizeof(Smem) <= 48 * 1024, "raster smem must fit the default 48 KB
 
 static_assert(sizeof(RegionSmem) <= 48 * 1024, "region smem must fit the default 48 KB limit");
 
-// T <= kChunk: the region kernel (one list per 2 x 2 tiles); otherwise the
-// tile kernel with chunked lists.
+// SMs of the current device (cached per device).
+static int device_sms() {
+  static std::atomic<int> sms[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
+  int n = sms[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    sms[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+// The region kernel when the whole list fits one chunk (T <= kChunk) and the
+// launch spans at least two full waves of its CTAs (4 per SM): a region CTA
+// works 4 tiles, so with fewer CTAs the slowest one sets the time and the
+// tile kernel's 4x finer grid is faster. Otherwise the tile kernel.
 template <int Mode, int kPrec>
 static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
-  if (a.T <= kChunk) {
-    const long long n_ctas = (long long)((a.tiles_x + 1) / 2) * ((a.tile_rows + 1) / 2) * a.B;
+  const long long n_ctas = (long long)((a.tiles_x + 1) / 2) * ((a.tile_rows + 1) / 2) * a.B;
+  if (a.T <= kChunk && n_ctas >= 8LL * device_sms()) {
     if (n_ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     dr_raster_region_kernel<Mode, kPrec><<<(unsigned)n_ctas, kThreads, sizeof(RegionSmem), s>>>(a);
     return cudaGetLastError();

@@ -257,12 +257,86 @@ def render(params: torch.Tensor, height: int, width: int, sigma: float, backgrou
     return out
 
 
+# Host-buffer calls: a copy stream and two compute streams per device.
+_side: dict[int, tuple] = {}
+
+
+def _side_streams(dev: torch.device):
+    s = _side.get(dev.index)
+    if s is None:
+        with _lock:
+            s = _side.get(dev.index)
+            if s is None:
+                s = (torch.cuda.Stream(device=dev),
+                     (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)))
+                _side[dev.index] = s
+    return s
+
+
+def _loss_backward_from_host(params: torch.Tensor, targets: torch.Tensor, sigma: float,
+                             background, layout: int, dev: torch.device):
+    """dr_loss_backward on host tensors, pipelined over scene chunks.
+
+    Scenes are independent, so the batch is cut into up to four chunks. Each
+    chunk's upload runs on a copy stream. Its kernel waits only for that upload
+    and runs on one of two compute streams, so chunk c computes while chunk
+    c + 1 uploads, and the tail of one chunk's kernel overlaps the next.
+    Results stay on the device; the caller's stream waits for all chunks.
+    """
+    p = params.detach().to(torch.float32).contiguous()
+    t = targets.detach().to(torch.float32).contiguous()
+    B, T = p.shape[0], p.shape[1]
+    if layout == LAYOUT_BCHW:
+        H, W = t.shape[2], t.shape[3]
+    else:
+        H, W = t.shape[1], t.shape[2]
+    cur = torch.cuda.current_stream(dev)
+    copy_s, comp = _side_streams(dev)
+    p_d = torch.empty(p.shape, dtype=torch.float32, device=dev)
+    t_d = torch.empty(t.shape, dtype=torch.float32, device=dev)
+    grads = torch.empty((B, T, N_PARAMS), dtype=torch.float32, device=dev)
+    losses = torch.empty((B,), dtype=torch.float32, device=dev)
+    bg, per = _bg_host(background, B)
+    # Work the caller already queued (on these buffers' memory) comes first.
+    copy_s.wait_stream(cur)
+    for s in comp:
+        s.wait_stream(cur)
+    n_chunks = min(4, B)
+    step = -(-B // n_chunks)
+    for c, lo in enumerate(range(0, B, step)):
+        hi = min(B, lo + step)
+        with torch.cuda.stream(copy_s):
+            p_d[lo:hi].copy_(p[lo:hi], non_blocking=True)
+            t_d[lo:hi].copy_(t[lo:hi], non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(copy_s)
+        s = comp[c % 2]
+        s.wait_event(ready)
+        bg_c = bg[3 * lo:3 * hi] if per else bg
+        check(lib().dr_loss_backward(context(dev, s.cuda_stream), _ptr(p_d[lo:hi]), _ptr(bg_c),
+                                     per, hi - lo, T, H, W, sigma, _ptr(t_d[lo:hi]), layout,
+                                     _ptr(grads[lo:hi]), _ptr(losses[lo:hi]), None,
+                                     ctypes.c_void_p(s.cuda_stream)))
+    for s in comp:
+        cur.wait_stream(s)
+    for buf in (p_d, t_d, grads, losses):
+        for s in (copy_s,) + comp:
+            buf.record_stream(s)
+    return losses, grads
+
+
 def loss_backward(params: torch.Tensor, targets: torch.Tensor, sigma: float,
                   background=(0.0, 0.0, 0.0), layout: int = LAYOUT_BHWC, want_image: bool = False,
                   device: torch.device | None = None):
-    """dr_loss_backward. Returns (losses (B,), grads (B,T,10)[, image])."""
+    """dr_loss_backward. Returns (losses (B,), grads (B,T,10)[, image]).
+
+    With host tensors (and no image requested) the upload is pipelined with
+    the computation over scene chunks (_loss_backward_from_host)."""
     sigma = _check_sigma(sigma)
     dev = _resolve_device(device if device is not None else params.device)
+    if (not want_image and not params.is_cuda and not targets.is_cuda and params.dim() == 3
+            and params.shape[0] > 1 and params.shape[1] > 0):
+        return _loss_backward_from_host(params, targets, sigma, background, layout, dev)
     p = _as_cuda_f32(params, dev)
     t = _as_cuda_f32(targets, dev)
     B, T = p.shape[0], p.shape[1]
