@@ -415,7 +415,15 @@ dr_status dr_mse_loss(dr_ctx* ctx, const float* images, const float* targets, in
   std::lock_guard<std::mutex> lock(ctx->mu);
   DeviceGuard g(ctx->device);
   if (B == 0) return DR_OK;
-  DR_CUDA(launch_mse(images, targets, B, (long long)n_per_image, losses, (cudaStream_t)stream),
+  const int nb = B < 65535 ? B : 65535;  // batches beyond this run in slices
+  dr_status st = ensure(ctx, ctx->partials,
+                        sizeof(double) * (size_t)nb * mse_partials_per_image(n_per_image), false);
+  if (st) return st;
+  st = ensure(ctx, ctx->counters, sizeof(unsigned) * (size_t)nb, true);
+  if (st) return st;
+  DR_CUDA(launch_mse(images, targets, B, (long long)n_per_image, losses,
+                     (double*)ctx->partials.ptr, (unsigned*)ctx->counters.ptr,
+                     (cudaStream_t)stream),
           "mse kernel");
   return DR_OK;
 }

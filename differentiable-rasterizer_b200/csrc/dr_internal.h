@@ -77,8 +77,11 @@ size_t tri_rec_bytes();
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
                          int tape_semantics, TriRec* recs, cudaStream_t s);
 cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s);
+// Per-image MSE scratch: B * mse_partials_per_image(n) doubles and B counters
+// (zero between launches; the kernel leaves them zero).
+size_t mse_partials_per_image(long long n);
 cudaError_t launch_mse(const float* img, const float* tgt, int B, long long n, float* losses,
-                       cudaStream_t s);
+                       double* partials, unsigned* counters, cudaStream_t s);
 cudaError_t launch_adam(const AdamArgs& a, cudaStream_t s);
 
 }  // namespace dr

@@ -58,10 +58,9 @@ __device__ __forceinline__ long long box_hi(float f, int n) {
   return v < n ? v : n;
 }
 
-__global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W, int H, float sigma,
-                                int tape_semantics, TriRec* __restrict__ recs) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= BT) return;
+// The record of triangle i (one scene-major index over the batch).
+__device__ __forceinline__ TriRec make_record(const float* __restrict__ params, int i, int W, int H,
+                                              float sigma, int tape_semantics) {
   const float* p = params + (size_t)i * kParams;
   float v[6];
 #pragma unroll
@@ -161,11 +160,30 @@ __global__ void dr_setup_kernel(const float* __restrict__ params, int BT, int W,
   r.pad = 0.0f;
   if (fast) flags |= kFastOk;
   r.flags = flags;
+  return r;
+}
 
-  float4* dst = reinterpret_cast<float4*>(recs + i);
-  const float4* src = reinterpret_cast<const float4*>(&r);
+// One thread per (scene, triangle). Records are staged in shared memory and
+// written as one contiguous run per block: a thread writing its own 176-byte
+// record would leave every 16-byte store to a different, partly written sector.
+constexpr int kSetupThreads = 128;
+__global__ void __launch_bounds__(kSetupThreads) dr_setup_kernel(
+    const float* __restrict__ params, int BT, int W, int H, float sigma, int tape_semantics,
+    TriRec* __restrict__ recs) {
+  constexpr int kQ = kRecWords / 4;  // float4s per record
+  __shared__ float4 stage[kSetupThreads * kQ];
+  const int first = blockIdx.x * kSetupThreads;
+  const int i = first + (int)threadIdx.x;
+  if (i < BT) {
+    const TriRec r = make_record(params, i, W, H, sigma, tape_semantics);
+    const float4* src = reinterpret_cast<const float4*>(&r);
 #pragma unroll
-  for (int j = 0; j < kRecWords / 4; ++j) dst[j] = src[j];
+    for (int j = 0; j < kQ; ++j) stage[threadIdx.x * kQ + j] = src[j];
+  }
+  __syncthreads();
+  const int n_here = min(kSetupThreads, BT - first);
+  float4* dst = reinterpret_cast<float4*>(recs + first);
+  for (int k = threadIdx.x; k < n_here * kQ; k += kSetupThreads) dst[k] = stage[k];
 }
 
 // ---------------------------------------------------------------------------
@@ -1292,50 +1310,119 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArg
 // MSE (canvas.rs:45-59) and Adam (optim.rs:40-60 + fit.rs:399-424)
 // ---------------------------------------------------------------------------
 
+// One block per (chunk of kMseChunk values, image): f32 differences squared
+// and summed in f64 (canvas.rs:45-59). Each block writes its partial; the
+// image's last block sums the partials in chunk order, so the result does not
+// depend on block scheduling.
+constexpr int kMseChunk = 8192;
 __global__ void dr_mse_kernel(const float* __restrict__ img, const float* __restrict__ tgt,
-                              long long n, float* __restrict__ losses) {
+                              long long n, int vec, double* __restrict__ partials,
+                              unsigned* __restrict__ counters, float* __restrict__ losses) {
   __shared__ double part[32];  // one per warp of a block of up to 1024 threads
-  const float* x = img + (size_t)blockIdx.x * n;
-  const float* y = tgt + (size_t)blockIdx.x * n;
+  __shared__ int is_last;
+  const int b = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n_warps = (int)(blockDim.x >> 5);
+  const long long c0 = (long long)blockIdx.x * kMseChunk;
+  const long long c1 = min(c0 + (long long)kMseChunk, n);
+  const float* x = img + (size_t)b * n;
+  const float* y = tgt + (size_t)b * n;
   double s = 0.0;
-  for (long long i = threadIdx.x; i < n; i += blockDim.x) {
-    double d = (double)__fsub_rn(x[i], y[i]);
-    s += d * d;
+  if (vec) {  // n % 4 == 0 and 16-byte aligned images: chunks start on float4s
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const float4* y4 = reinterpret_cast<const float4*>(y);
+    for (long long i = c0 / 4 + threadIdx.x; i < c1 / 4; i += blockDim.x) {
+      const float4 u = x4[i], w = y4[i];
+      const double d0 = (double)__fsub_rn(u.x, w.x), d1 = (double)__fsub_rn(u.y, w.y);
+      const double d2 = (double)__fsub_rn(u.z, w.z), d3 = (double)__fsub_rn(u.w, w.w);
+      s += d0 * d0 + d1 * d1 + d2 * d2 + d3 * d3;
+    }
+  } else {
+    for (long long i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+      const double d = (double)__fsub_rn(x[i], y[i]);
+      s += d * d;
+    }
   }
   s = warp_sum_d(s);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  if (lane == 0) part[warp] = s;
   __syncthreads();
   if (threadIdx.x == 0) {
     double t = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
-    losses[blockIdx.x] = (float)(t / (double)n);
+    for (int w = 0; w < n_warps; ++w) t += part[w];
+    partials[(size_t)b * gridDim.x + blockIdx.x] = t;
+    __threadfence();
+    is_last = atomicAdd(&counters[b], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  double t = 0.0;
+  for (unsigned i = threadIdx.x; i < gridDim.x; i += blockDim.x)
+    t += *((volatile double*)&partials[(size_t)b * gridDim.x + i]);
+  t = warp_sum_d(t);
+  __syncthreads();  // part[] above has been read
+  if (lane == 0) part[warp] = t;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double tot = 0.0;
+    for (int w = 0; w < n_warps; ++w) tot += part[w];
+    losses[b] = (float)(tot / (double)n);
+    counters[b] = 0;
   }
 }
 
-__global__ void dr_adam_kernel(AdamArgs a) {
-  if (a.skip_flag && *a.skip_flag) return;
-  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= a.n) return;
-  if (a.copy_flag && *a.copy_flag) a.copy_dst[i] = a.params[i];
-  if (a.run_flag && !*a.run_flag) return;
+// Adam::step for element i (optim.rs:40-60) with fit.rs's per-parameter rate
+// and projection; IEEE division and square root as the reference rounds them.
+__device__ __forceinline__ float adam_one(const AdamArgs& a, long long i, float p, float g,
+                                          float& m, float& v) {
   const int cls = (int)(i % kParams);
   const float lr = cls < 6 ? a.lr_pos : (cls < 9 ? a.lr_color : a.lr_alpha);
-  float g = a.grads[i];
-  float m = __fadd_rn(__fmul_rn(a.beta1, a.m[i]), __fmul_rn(a.one_minus_beta1, g));
-  float v = __fadd_rn(__fmul_rn(a.beta2, a.v[i]), __fmul_rn(__fmul_rn(a.one_minus_beta2, g), g));
-  a.m[i] = m;
-  a.v[i] = v;
-  float m_hat = __fdiv_rn(m, a.bc1);
-  float v_hat = __fdiv_rn(v, a.bc2);
-  float p = __fsub_rn(a.params[i],
-                      __fdiv_rn(__fmul_rn(lr, m_hat), __fadd_rn(__fsqrt_rn(v_hat), a.eps)));
+  m = __fadd_rn(__fmul_rn(a.beta1, m), __fmul_rn(a.one_minus_beta1, g));
+  v = __fadd_rn(__fmul_rn(a.beta2, v), __fmul_rn(__fmul_rn(a.one_minus_beta2, g), g));
+  const float m_hat = __fdiv_rn(m, a.bc1);
+  const float v_hat = __fdiv_rn(v, a.bc2);
+  p = __fsub_rn(p, __fdiv_rn(__fmul_rn(lr, m_hat), __fadd_rn(__fsqrt_rn(v_hat), a.eps)));
   if (a.project) {
     if (p != p) p = 0.5f;
     if (cls < 6) p = rclamp(p, -0.25f, 1.25f);
     else if (cls < 9) p = rclamp(p, 0.0f, 1.0f);
     else p = rclamp(p, 1e-3f, 0.999f);
   }
+  return p;
+}
+
+__global__ void dr_adam_kernel(AdamArgs a) {
+  if (a.skip_flag && *a.skip_flag) return;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.n) return;
+  if (a.copy_flag && *a.copy_flag) a.copy_dst[i] = a.params[i];
+  if (a.run_flag && !*a.run_flag) return;
+  float m = a.m[i], v = a.v[i];
+  const float p = adam_one(a, i, a.params[i], a.grads[i], m, v);
+  a.m[i] = m;
+  a.v[i] = v;
   a.params[i] = p;
+}
+
+// Four consecutive elements per thread with 16-byte loads and stores (n a
+// multiple of 4, every array 16-byte aligned); the same per-element update.
+__global__ void dr_adam4_kernel(AdamArgs a) {
+  if (a.skip_flag && *a.skip_flag) return;
+  const long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q * 4 >= a.n) return;
+  float4 P = reinterpret_cast<const float4*>(a.params)[q];
+  if (a.copy_flag && *a.copy_flag) reinterpret_cast<float4*>(a.copy_dst)[q] = P;
+  if (a.run_flag && !*a.run_flag) return;
+  const float4 G = reinterpret_cast<const float4*>(a.grads)[q];
+  float4 M = reinterpret_cast<const float4*>(a.m)[q];
+  float4 V = reinterpret_cast<const float4*>(a.v)[q];
+  const long long i = q * 4;
+  P.x = adam_one(a, i, P.x, G.x, M.x, V.x);
+  P.y = adam_one(a, i + 1, P.y, G.y, M.y, V.y);
+  P.z = adam_one(a, i + 2, P.z, G.z, M.z, V.z);
+  P.w = adam_one(a, i + 3, P.w, G.w, M.w, V.w);
+  reinterpret_cast<float4*>(a.m)[q] = M;
+  reinterpret_cast<float4*>(a.v)[q] = V;
+  reinterpret_cast<float4*>(a.params)[q] = P;
 }
 
 // ---------------------------------------------------------------------------
@@ -1410,9 +1497,8 @@ cudaError_t launch_fit_control(FitState* st, int iter, float min_delta, long lon
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
                          int tape_semantics, TriRec* recs, cudaStream_t s) {
   if (BT == 0) return cudaSuccess;
-  int threads = 128;
-  int blocks = (BT + threads - 1) / threads;
-  dr_setup_kernel<<<blocks, threads, 0, s>>>(params, BT, W, H, sigma, tape_semantics, recs);
+  const int blocks = (BT + kSetupThreads - 1) / kSetupThreads;
+  dr_setup_kernel<<<blocks, kSetupThreads, 0, s>>>(params, BT, W, H, sigma, tape_semantics, recs);
   return cudaGetLastError();
 }
 
@@ -1481,18 +1567,41 @@ cudaError_t launch_raster(int mode, const RasterArgs& args, int n_tiles, cudaStr
   return cudaErrorInvalidValue;
 }
 
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+size_t mse_partials_per_image(long long n) { return (size_t)((n + kMseChunk - 1) / kMseChunk); }
+
+// partials: B * mse_partials_per_image(n) doubles; counters: B, zero between launches.
 cudaError_t launch_mse(const float* img, const float* tgt, int B, long long n, float* losses,
-                       cudaStream_t s) {
+                       double* partials, unsigned* counters, cudaStream_t s) {
   if (B == 0) return cudaSuccess;
-  dr_mse_kernel<<<B, 512, 0, s>>>(img, tgt, n, losses);
-  return cudaGetLastError();
+  if (n == 0) return cudaMemsetAsync(losses, 0xff, sizeof(float) * (size_t)B, s);  // 0/0: NaN
+  const unsigned chunks = (unsigned)mse_partials_per_image(n);
+  static_assert(kMseChunk % 4 == 0, "float4 chunks");
+  const int vec = n % 4 == 0 && aligned16(img) && aligned16(tgt);
+  for (int b0 = 0; b0 < B; b0 += 65535) {  // gridDim.y limit
+    const int nb = min(B - b0, 65535);
+    dim3 grid(chunks, nb);
+    dr_mse_kernel<<<grid, 256, 0, s>>>(img + (size_t)b0 * n, tgt + (size_t)b0 * n, n, vec,
+                                       partials, counters, losses + b0);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_adam(const AdamArgs& a, cudaStream_t s) {
   if (a.n == 0) return cudaSuccess;
-  int threads = 256;
-  long long blocks = (a.n + threads - 1) / threads;
-  dr_adam_kernel<<<(unsigned)blocks, threads, 0, s>>>(a);
+  const int threads = 256;
+  const bool vec = a.n % 4 == 0 && aligned16(a.params) && aligned16(a.m) && aligned16(a.v) &&
+                   aligned16(a.grads) && (!a.copy_dst || aligned16(a.copy_dst));
+  if (vec) {
+    const long long blocks = (a.n / 4 + threads - 1) / threads;
+    dr_adam4_kernel<<<(unsigned)blocks, threads, 0, s>>>(a);
+  } else {
+    const long long blocks = (a.n + threads - 1) / threads;
+    dr_adam_kernel<<<(unsigned)blocks, threads, 0, s>>>(a);
+  }
   return cudaGetLastError();
 }
 

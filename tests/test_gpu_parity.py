@@ -268,12 +268,27 @@ def test_mse_kernel_matches_oracle(native, oracle):
         assert abs(got[i] - oracle.mse(a[i], b[i])) <= 1e-7 * abs(got[i])
 
 
-def test_adam_is_bit_exact(native, oracle):
+@pytest.mark.parametrize("shape", [(1, 1, 1, 3), (4, 5, 7, 3), (2, 301, 257, 3), (40, 64, 64, 3)])
+def test_mse_kernel_sizes_and_determinism(native, oracle, shape):
+    # One chunk, many chunks with a ragged last chunk, and many images; the
+    # chunk partials are summed in a fixed order, so repeated calls agree bitwise.
+    rng = np.random.default_rng(sum(shape))
+    a = rng.uniform(-1, 2, shape).astype(np.float32)
+    b = rng.uniform(-1, 2, shape).astype(np.float32)
+    first = host(native.mse_loss(cuda(a), cuda(b)))
+    again = host(native.mse_loss(cuda(a), cuda(b)))
+    assert np.array_equal(first, again)
+    ref = np.array([oracle.mse(a[i], b[i]) for i in range(shape[0])], np.float32)
+    np.testing.assert_allclose(first, ref, rtol=1e-7, atol=0)
+
+
+@pytest.mark.parametrize("tris", [97, 96])  # scalar kernel (n % 4 != 0) and the float4 kernel
+def test_adam_is_bit_exact(native, oracle, tris):
     rng = np.random.default_rng(4)
-    n = 10 * 97
+    n = 10 * tris
     p0 = rng.uniform(-0.5, 1.5, n).astype(np.float32)
     p0[5] = np.nan
-    lr = oracle.learning_rates(97)
+    lr = oracle.learning_rates(tris)
     adam = oracle.Adam(n)
     p_ref = p0.copy()
     P, M, V = cuda(p0), torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
