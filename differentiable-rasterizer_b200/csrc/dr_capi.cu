@@ -90,8 +90,9 @@ struct dr_ctx {
   std::mutex mu;
   int bg_on_device = 0;
   int precision = 0;
+  int split_blocks = 0;  // dr_set_triangle_split: 0 automatic, 1 never, k exactly
   uint64_t hits = 0, misses = 0;
-  Slot recs, partials, counters, bgbuf;
+  Slot recs, partials, counters, bgbuf, split;
   // fit state
   Slot fit_params, fit_m, fit_v, fit_grads, fit_losses, fit_state;
   cudaStream_t capture_stream = nullptr;
@@ -137,8 +138,8 @@ dr_status ensure(dr_ctx* c, Slot& s, size_t bytes, bool zero) {
 
 uint64_t pool_bytes(dr_ctx* c) {
   uint64_t b = 0;
-  for (Slot* s : {&c->recs, &c->partials, &c->counters, &c->bgbuf, &c->fit_params, &c->fit_m,
-                  &c->fit_v, &c->fit_grads, &c->fit_losses, &c->fit_state})
+  for (Slot* s : {&c->recs, &c->partials, &c->counters, &c->bgbuf, &c->split, &c->fit_params,
+                  &c->fit_m, &c->fit_v, &c->fit_grads, &c->fit_losses, &c->fit_state})
     b += s->cap;
   return b;
 }
@@ -263,6 +264,17 @@ dr_status backward_common(dr_ctx* ctx, int mode, const float* params, const floa
     st = loss_scratch(ctx, a, n_tiles);
     if (st) return st;
   }
+  // Too few tiles to fill the GPU: split each pixel's chain into triangle
+  // blocks (all tile rows only).
+  const int k = n_shards > 1 ? 1
+                : ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(B, T, n_tiles);
+  if (k > 1) {
+    st = ensure(ctx, ctx->split, raster_split_bytes(B, k, H, W), false);
+    if (st) return st;
+    DR_CUDA(launch_raster_split(mode, a, n_tiles, k, (float4*)ctx->split.ptr, s),
+            "split raster kernels");
+    return DR_OK;
+  }
   DR_CUDA(launch_raster(mode, a, n_tiles, s), "raster kernel");
   return DR_OK;
 }
@@ -330,8 +342,8 @@ dr_status dr_ctx_destroy(dr_ctx* c) {
   {
     DeviceGuard g(c->device);
     cudaDeviceSynchronize();
-    for (Slot* s : {&c->recs, &c->partials, &c->counters, &c->bgbuf, &c->fit_params, &c->fit_m,
-                    &c->fit_v, &c->fit_grads, &c->fit_losses, &c->fit_state})
+    for (Slot* s : {&c->recs, &c->partials, &c->counters, &c->bgbuf, &c->split, &c->fit_params,
+                    &c->fit_m, &c->fit_v, &c->fit_grads, &c->fit_losses, &c->fit_state})
       free_slot(*s);
     if (c->fit_exec) cudaGraphExecDestroy(c->fit_exec);
     if (c->capture_stream) cudaStreamDestroy(c->capture_stream);
@@ -343,6 +355,20 @@ dr_status dr_ctx_destroy(dr_ctx* c) {
 dr_status dr_set_background_location(dr_ctx* ctx, int on_device) {
   if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
   ctx->bg_on_device = on_device ? 1 : 0;
+  return DR_OK;
+}
+
+dr_status dr_set_triangle_split(dr_ctx* ctx, int blocks) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (blocks < 0 || blocks > 65535)
+    return fail(DR_INVALID_ARGUMENT, "triangle blocks must be in [0, 65535], got %d", blocks);
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  ctx->split_blocks = blocks;
+  if (ctx->fit_exec) {
+    cudaGraphExecDestroy(ctx->fit_exec);
+    ctx->fit_exec = nullptr;
+    ctx->fit_key.clear();
+  }
   return DR_OK;
 }
 
@@ -484,8 +510,9 @@ dr_status dr_clear_pool(dr_ctx* ctx) {
   std::lock_guard<std::mutex> lock(ctx->mu);
   DeviceGuard g(ctx->device);
   cudaDeviceSynchronize();
-  for (Slot* s : {&ctx->recs, &ctx->partials, &ctx->counters, &ctx->bgbuf, &ctx->fit_params,
-                  &ctx->fit_m, &ctx->fit_v, &ctx->fit_grads, &ctx->fit_losses, &ctx->fit_state})
+  for (Slot* s : {&ctx->recs, &ctx->partials, &ctx->counters, &ctx->bgbuf, &ctx->split,
+                  &ctx->fit_params, &ctx->fit_m, &ctx->fit_v, &ctx->fit_grads, &ctx->fit_losses,
+                  &ctx->fit_state})
     free_slot(*s);
   if (ctx->fit_exec) {
     cudaGraphExecDestroy(ctx->fit_exec);
@@ -564,6 +591,9 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
   if ((st = ensure(ctx, ctx->fit_losses, (size_t)std::max(iters, 1) * 4, false))) return st;
   if ((st = ensure(ctx, ctx->fit_state, sizeof(FitState), true))) return st;
   int tiles = ((W + kTileSide - 1) / kTileSide) * ((H + kTileSide - 1) / kTileSide);
+  const int split_k = ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(1, T, tiles);
+  if (split_k > 1 && (st = ensure(ctx, ctx->split, raster_split_bytes(1, split_k, H, W), false)))
+    return st;
   if ((st = ensure(ctx, ctx->recs, tri_rec_bytes() * (size_t)T, false))) return st;
   if ((st = ensure(ctx, ctx->partials, sizeof(double) * (size_t)tiles, false))) return st;
   if ((st = ensure(ctx, ctx->counters, sizeof(unsigned), true))) return st;
@@ -582,7 +612,7 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
     key.insert(key.end(), b, b + n);
   };
   const void* ptrs[] = {target, init_params, best_params, final_params, P, M, V, Gr, L, S,
-                        ctx->recs.ptr, ctx->partials.ptr, ctx->counters.ptr};
+                        ctx->recs.ptr, ctx->partials.ptr, ctx->counters.ptr, ctx->split.ptr};
   push(ptrs, sizeof(ptrs));
   push(cfg, sizeof(*cfg));
   int dims[3] = {H, W, T};
@@ -637,7 +667,10 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       a.losses = &S->loss;
       a.n_values = (double)H * (double)W * 3.0;
       a.skip_flag = &S->stopped;
-      chk(launch_raster(kModeLoss, a, tiles, cs));
+      if (split_k > 1)
+        chk(launch_raster_split(kModeLoss, a, tiles, split_k, (float4*)ctx->split.ptr, cs));
+      else
+        chk(launch_raster(kModeLoss, a, tiles, cs));
       chk(launch_fit_control(S, i, cfg->min_delta, cfg->patience, L, cs));
       AdamArgs ad;
       memset(&ad, 0, sizeof(ad));

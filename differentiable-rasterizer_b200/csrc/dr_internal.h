@@ -10,7 +10,10 @@ namespace dr {
 
 struct TriRec;
 
-enum RasterMode { kModeRender = 0, kModeLoss = 1, kModeGrad = 2 };
+enum RasterMode { kModeRender = 0, kModeLoss = 1, kModeGrad = 2,
+                  // Triangle-block split (launch_raster_split): per (tile, block) forward
+                  // over black, then the per-block gradient pass.
+                  kModeSplitFwd = 3, kModeSplitBwd = 4 };
 enum Layout { kLayoutBHWC = 0, kLayoutBCHW = 1 };
 
 struct RasterArgs {
@@ -36,6 +39,8 @@ struct RasterArgs {
   double* loss_sums;          // optional (B,) sum of squared error
   double n_values;            // H*W*3
   const int* skip_flag;       // optional: nonzero -> the kernel does nothing
+  int split_k;                // triangle blocks of a split launch (else 0)
+  float4* split;              // split state: 4 float4 per (scene, block, pixel)
 };
 
 struct AdamArgs {
@@ -77,6 +82,21 @@ size_t tri_rec_bytes();
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
                          int tape_semantics, TriRec* recs, cudaStream_t s);
 cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s);
+// Triangle blocks for a loss/grad launch over all tile rows of B scenes: 1 when
+// the plain launch fills the GPU, else up to 8 (at least 32 triangles each).
+int raster_split_blocks(int B, int T, int n_tiles);
+// Bytes of split state a launch with k blocks needs (4 float4 per scene, block
+// and pixel).
+inline size_t raster_split_bytes(int B, int k, int H, int W) {
+  return (size_t)B * k * H * W * 4 * sizeof(float4);
+}
+// kModeLoss / kModeGrad as three launches over k triangle blocks: forward per
+// (tile, block) over black, a per-pixel combine of the blocks' affine maps
+// (final colour, loss, canvas entering each block, attenuation from the blocks
+// above), then the gradient pass per (tile, block). All tile rows (row0 0,
+// step 1).
+cudaError_t launch_raster_split(int mode, const RasterArgs& a, int n_tiles, int k, float4* split,
+                                cudaStream_t s);
 // Per-image MSE scratch: B * mse_partials_per_image(n) doubles and B counters
 // (zero between launches; the kernel leaves them zero).
 size_t mse_partials_per_image(long long n);

@@ -1157,13 +1157,23 @@ __device__ __forceinline__ void scene_loss(const RasterArgs& a, int b, int slot,
   }
 }
 
-// Tile kernel: one CTA per (scene, 16x16 tile), warp w on block w; lists
-// longer than kChunk are binned in chunks behind barriers.
+// Split state of one pixel of one triangle block: [c0 c1 c2 m] [e z0 zn -]
+// written by the block's forward (composite over black, running product),
+// then [g0 g1 g2 -] [d0 d1 d2 -] written by the combine (the gradient reaching
+// the block, the canvas entering it).
+__device__ __forceinline__ float4* split_pixel(const RasterArgs& a, int b, int kblk, int px,
+                                               int py) {
+  return a.split + ((size_t)(b * a.split_k + kblk) * a.H * a.W + (size_t)py * a.W + px) * 4;
+}
+
+// Tile kernel: one CTA per (scene, 16x16 tile[, triangle block]), warp w on
+// block w; lists longer than kChunk are binned in chunks behind barriers.
 template <int Mode, int kPrec>
 __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   if (a.skip_flag && *a.skip_flag) return;
+  constexpr bool kSplit = Mode == kModeSplitFwd || Mode == kModeSplitBwd;
 
   const int b = blockIdx.y;
   const int local_tile = blockIdx.x;
@@ -1179,39 +1189,74 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   Consts K;
   K.sigma_eff = a.sigma_eff;
   K.inv_sigma = a.inv_sigma;
-  const int n_chunks = (a.T + kChunk - 1) / kChunk;
-
-  // ---- pass 1: forward composite ------------------------------------------
-  float c0, c1, c2;
-  scene_background(a, b, c0, c1, c2);
+  // Triangles [t0, t1): all of them, or this CTA's block of a split launch.
+  int t0 = 0, t1 = a.T;
+  if (kSplit) {
+    const int per = (a.T + a.split_k - 1) / a.split_k;
+    t0 = min(a.T, (int)blockIdx.z * per);
+    t1 = min(a.T, t0 + per);
+  }
+  const int n_chunks = (t1 - t0 + kChunk - 1) / kChunk;
+  int count = 0;
   Prod P;
   P.init();
-  int count = 0;
-  for (int ci = 0; ci < n_chunks; ++ci) {
-    count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H);
-    forward_walk<Mode, kPrec>(sm, count, warp, px, py, ptx, pty, active, K, c0, c1, c2, P);
-  }
-  if (a.image && active) store_pixel(a, b, px, py, c0, c1, c2);
-  if (Mode == kModeRender) return;
+  float G0 = 0.0f, G1 = 0.0f, G2 = 0.0f;
+  float r0, r1, r2;
 
-  // ---- loss and the gradient reaching the top of the stack ----------------
-  float G0, G1, G2;
-  double sq;
-  top_gradient<Mode>(a, b, px, py, active, c0, c1, c2, G0, G1, G2, sq);
-  if (Mode == kModeLoss) {
-    const double ws = warp_sum_d(sq);
-    if (lane == 0) sm.loss_part[warp] = ws;
+  if (Mode != kModeSplitBwd) {
+    // ---- pass 1: forward composite ----------------------------------------
+    float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;  // a block composites over black
+    if (!kSplit) scene_background(a, b, c0, c1, c2);
+    for (int ci = 0; ci < n_chunks; ++ci) {
+      count = build_list(sm, recs, t1, t0 + ci * kChunk, tx0, ty0, a.W, a.H);
+      forward_walk<Mode, kPrec>(sm, count, warp, px, py, ptx, pty, active, K, c0, c1, c2, P);
+    }
+    if (Mode == kModeSplitFwd) {
+      if (active) {
+        float4* sp = split_pixel(a, b, blockIdx.z, px, py);
+        sp[0] = make_float4(c0, c1, c2, P.m);
+        sp[1] = make_float4(__int_as_float(P.e), __int_as_float(P.z0), __int_as_float(P.zn), 0.f);
+      }
+      return;
+    }
+    if (a.image && active) store_pixel(a, b, px, py, c0, c1, c2);
+    if (Mode == kModeRender) return;
+
+    // ---- loss and the gradient reaching the top of the stack --------------
+    double sq;
+    top_gradient<Mode>(a, b, px, py, active, c0, c1, c2, G0, G1, G2, sq);
+    if (Mode == kModeLoss) {
+      const double ws = warp_sum_d(sq);
+      if (lane == 0) sm.loss_part[warp] = ws;
+    }
+    scene_background(a, b, r0, r1, r2);
+  } else {
+    // The block's running product from its forward, and from the combine the
+    // gradient reaching the block and the canvas entering it.
+    r0 = r1 = r2 = 0.0f;
+    if (active) {
+      const float4* sp = split_pixel(a, b, blockIdx.z, px, py);
+      const float4 s0 = sp[0], s1 = sp[1], s2 = sp[2], s3 = sp[3];
+      P.m = s0.w;
+      P.e = __float_as_int(s1.x);
+      P.z0 = __float_as_int(s1.y);
+      P.zn = __float_as_int(s1.z);
+      G0 = s2.x;
+      G1 = s2.y;
+      G2 = s2.z;
+      r0 = s3.x;
+      r1 = s3.y;
+      r2 = s3.z;
+    }
   }
 
   // ---- pass 2: recomposite in forward order and accumulate gradients ------
-  float r0, r1, r2;
-  scene_background(a, b, r0, r1, r2);
   Prod Q;
   Q.init();
   for (int ci = 0; ci < n_chunks; ++ci) {
-    if (n_chunks > 1) {
+    if (n_chunks > 1 || Mode == kModeSplitBwd) {
       __syncthreads();
-      count = build_list(sm, recs, a.T, ci * kChunk, tx0, ty0, a.W, a.H);
+      count = build_list(sm, recs, t1, t0 + ci * kChunk, tx0, ty0, a.W, a.H);
     }
     for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
     __syncthreads();
@@ -1223,6 +1268,82 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
 
   if (Mode == kModeLoss)
     scene_loss(a, b, blockIdx.x, gridDim.x, sm.loss_part, kWarps, sm.loss_part, &sm.is_last);
+}
+
+// Combine of a split launch, one thread per pixel (CTA = tile). Block k's
+// layers map the canvas beneath them to a_k x + c_k, a_k the product of their
+// (1 - w) (0 after an opaque layer, NaN after a NaN one, as the reference's
+// running composite propagates them) and c_k their composite over black. The
+// canvas entering block k is the composition of the maps below applied to the
+// background; the final colour is the composition of all. The gradient
+// reaching block k is G times the product of a_j over the blocks above.
+constexpr int kMaxSplit = 8;  // automatic splits use at most this many blocks
+
+template <int Mode>
+__global__ void __launch_bounds__(kThreads) dr_split_combine_kernel(RasterArgs a) {
+  __shared__ double loss_part[kWarps];
+  __shared__ int is_last;
+  if (a.skip_flag && *a.skip_flag) return;
+  const int b = blockIdx.y;
+  const int tile_col = blockIdx.x % a.tiles_x;
+  const int tile_row = a.tile_row0 + (blockIdx.x / a.tiles_x) * a.tile_row_step;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int px = tile_col * kTile + (warp & 1) * kBlockW + (lane & 7);
+  const int py = tile_row * kTile + (warp >> 1) * kBlockH + (lane >> 3);
+  const bool active = px < a.W && py < a.H;
+  double sq = 0.0;
+  if (active) {
+    float d0, d1, d2;
+    scene_background(a, b, d0, d1, d2);
+    // Block maps in registers for up to kMaxSplit blocks (all loads issued
+    // together); a forced larger split re-reads them.
+    float ak[kMaxSplit];
+    const int kk = a.split_k;
+#pragma unroll
+    for (int k = 0; k < kMaxSplit; ++k) {
+      if (k >= kk) break;
+      float4* sp = split_pixel(a, b, k, px, py);
+      const float4 s0 = __ldcg(sp), s1 = __ldcg(sp + 1);
+      const int e = __float_as_int(s1.x), z0 = __float_as_int(s1.y), zn = __float_as_int(s1.z);
+      ak[k] = zn >= 0 ? __int_as_float(0x7fc00000) : (z0 >= 0 ? 0.0f : ldexpf(s0.w, -64 * e));
+      sp[3] = make_float4(d0, d1, d2, ak[k]);
+      d0 = __fadd_rn(__fmul_rn(ak[k], d0), s0.x);
+      d1 = __fadd_rn(__fmul_rn(ak[k], d1), s0.y);
+      d2 = __fadd_rn(__fmul_rn(ak[k], d2), s0.z);
+    }
+    for (int k = kMaxSplit; k < kk; ++k) {
+      float4* sp = split_pixel(a, b, k, px, py);
+      const float4 s0 = sp[0], s1 = sp[1];
+      const int e = __float_as_int(s1.x), z0 = __float_as_int(s1.y), zn = __float_as_int(s1.z);
+      const float akk = zn >= 0 ? __int_as_float(0x7fc00000)
+                                : (z0 >= 0 ? 0.0f : ldexpf(s0.w, -64 * e));
+      sp[3] = make_float4(d0, d1, d2, akk);
+      d0 = __fadd_rn(__fmul_rn(akk, d0), s0.x);
+      d1 = __fadd_rn(__fmul_rn(akk, d1), s0.y);
+      d2 = __fadd_rn(__fmul_rn(akk, d2), s0.z);
+    }
+    if (a.image) store_pixel(a, b, px, py, d0, d1, d2);
+    float G0, G1, G2;
+    top_gradient<Mode>(a, b, px, py, true, d0, d1, d2, G0, G1, G2, sq);
+    float above = 1.0f;
+    for (int k = kk - 1; k >= kMaxSplit; --k) {
+      float4* sp = split_pixel(a, b, k, px, py);
+      sp[2] = make_float4(__fmul_rn(G0, above), __fmul_rn(G1, above), __fmul_rn(G2, above), 0.f);
+      above = __fmul_rn(above, sp[3].w);
+    }
+#pragma unroll
+    for (int k = kMaxSplit - 1; k >= 0; --k) {
+      if (k >= kk) continue;
+      float4* sp = split_pixel(a, b, k, px, py);
+      sp[2] = make_float4(__fmul_rn(G0, above), __fmul_rn(G1, above), __fmul_rn(G2, above), 0.f);
+      above = __fmul_rn(above, ak[k]);
+    }
+  }
+  if (Mode == kModeLoss) {
+    const double ws = warp_sum_d(sq);
+    if (lane == 0) loss_part[warp] = ws;
+    scene_loss(a, b, blockIdx.x, gridDim.x, loss_part, kWarps, loss_part, &is_last);
+  }
 }
 
 // k-th index of 0..n-1 in centre-out order: c, c-1, c+1, c-2, c+2, ...
@@ -1554,6 +1675,50 @@ static cudaError_t launch_prec(int mode, const RasterArgs& a, int n_tiles, cudaS
 
 // n_tiles: the 16x16 tiles per scene the launch covers (a.tiles_x per covered
 // tile row). Either kernel uses at most n_tiles loss partials per scene.
+int raster_split_blocks(int B, int T, int n_tiles) {
+  const long long ctas = (long long)B * n_tiles;
+  const int sms = device_sms();
+  if (ctas >= 2LL * sms || T < 64) return 1;
+  const long long want = (4LL * sms + ctas - 1) / ctas;
+  long long k = want < 8 ? want : 8;
+  if (k > T / 32) k = T / 32;
+  return k < 2 ? 1 : (int)k;
+}
+
+template <int kPrec>
+static cudaError_t launch_split_prec(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s) {
+  RasterArgs f = a;
+  f.image = nullptr;  // the combine writes the image
+  dim3 grid3(n_tiles, a.B, a.split_k), grid2(n_tiles, a.B);
+  dr_raster_kernel<kModeSplitFwd, kPrec><<<grid3, kThreads, sizeof(Smem), s>>>(f);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (mode == kModeLoss) dr_split_combine_kernel<kModeLoss><<<grid2, kThreads, 0, s>>>(a);
+  else dr_split_combine_kernel<kModeGrad><<<grid2, kThreads, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  dr_raster_kernel<kModeSplitBwd, kPrec><<<grid3, kThreads, sizeof(Smem), s>>>(f);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_raster_split(int mode, const RasterArgs& args, int n_tiles, int k, float4* split,
+                                cudaStream_t s) {
+  if (args.B == 0 || n_tiles == 0) return cudaSuccess;
+  if (args.tiles_x <= 0 || k < 1 || k > 65535 || !split ||
+      (mode != kModeLoss && mode != kModeGrad) || args.tile_row0 != 0 || args.tile_row_step != 1)
+    return cudaErrorInvalidValue;
+  RasterArgs a = args;
+  a.tile_rows = n_tiles / a.tiles_x;
+  a.split_k = k;
+  a.split = split;
+  switch (a.precision) {
+    case kPrecRef: return launch_split_prec<kPrecRef>(mode, a, n_tiles, s);
+    case kPrecStrict: return launch_split_prec<kPrecStrict>(mode, a, n_tiles, s);
+    case kPrecFast: return launch_split_prec<kPrecFast>(mode, a, n_tiles, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_raster(int mode, const RasterArgs& args, int n_tiles, cudaStream_t s) {
   if (args.B == 0 || n_tiles == 0) return cudaSuccess;
   if (args.tiles_x <= 0) return cudaErrorInvalidValue;

@@ -76,6 +76,7 @@ SIGNATURES = {
     "dr_device_count": (_I, []),
     "dr_set_background_location": (_I, [_P, _I]),
     "dr_set_precision": (_I, [_P, _I]),
+    "dr_set_triangle_split": (_I, [_P, _I]),
     "dr_render": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "dr_loss_backward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P, _P]),
     "dr_grad_backward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P]),
@@ -160,6 +161,8 @@ def context(device: torch.device, stream: int):
                 check(lib().dr_ctx_create(device.index, ctypes.byref(h)))
                 if _precision != PRECISION_REFERENCE:
                     check(lib().dr_set_precision(h, _precision))
+                if _split:
+                    check(lib().dr_set_triangle_split(h, _split))
                 _ctxs[key] = c = h
     return c
 
@@ -179,6 +182,19 @@ def set_precision(mode: int) -> None:
 
 def get_precision() -> int:
     return _precision
+
+
+_split = 0
+
+
+def set_triangle_split(blocks: int) -> None:
+    """Triangle-block split for every context (dr_set_triangle_split):
+    0 automatic, 1 never, k exactly k blocks."""
+    global _split
+    _split = int(blocks)
+    with _lock:
+        for h in _ctxs.values():
+            check(lib().dr_set_triangle_split(h, _split))
 
 
 def shutdown() -> bool:

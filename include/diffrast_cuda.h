@@ -110,6 +110,16 @@ typedef enum dr_precision {
 } dr_precision;
 DR_API dr_status dr_set_precision(dr_ctx* ctx, int precision);
 
+/* Triangle-block split of loss/gradient calls (dr_loss_backward,
+ * dr_grad_backward, dr_fit). When a call's scenes x 16x16 tiles are too few to
+ * fill the GPU (a small image, one scene), each pixel's compositing chain is
+ * cut into blocks of consecutive triangles. The blocks run as separate CTAs and
+ * their compositing maps are combined per pixel. 0 = choose automatically
+ * (default), 1 = never split, k >= 2 = exactly k blocks (at most 65535; calls
+ * sharded by tile rows never split). Results agree with the unsplit path to
+ * rounding. No reference counterpart. */
+DR_API dr_status dr_set_triangle_split(dr_ctx* ctx, int blocks);
+
 /* --- hot path ------------------------------------------------------------ */
 
 /* Forward render of a batch into `image` (layout as given).
