@@ -34,7 +34,9 @@ constexpr int kBlockW = 8, kBlockH = 4;                  // one warp's pixel blo
 constexpr int kWarps = (kTile / kBlockW) * (kTile / kBlockH);
 constexpr int kThreads = kWarps * 32;
 constexpr int kChunk = 128;                              // triangles binned per round (<= kThreads)
-constexpr int kRegionBlocks = 4 * kWarps;                // region kernel: 2 x 2 tiles
+constexpr int kBlocksPerTile = kWarps;                    // 2 columns x 4 rows of warp blocks
+constexpr int kRegionBlocks = 4 * kBlocksPerTile;        // region kernel: 2 x 2 tiles
+static_assert(kBlocksPerTile == 8, "tile block codes are stored as one 64-bit word");
 constexpr float kRenorm = 18446744073709551616.0f;        // 2^64
 constexpr float kRenormInv = 5.42101086242752217e-20f;    // 2^-64
 
@@ -190,11 +192,15 @@ __global__ void __launch_bounds__(kSetupThreads) dr_setup_kernel(
 // Raster kernel
 // ---------------------------------------------------------------------------
 //
-// One CTA per (scene, 16x16 tile), 4 warps; each warp owns an 8x8 block and
-// each lane two pixels of it (rows y and y + 4). Triangles are binned per
-// tile in order (build_list) and every kept (tile, triangle) entry carries a
-// 4-bit code per warp block, decided once at binning time from the block's
-// rectangle against the triangle's box and edge lines:
+// A warp owns an 8x4 block of pixels, one pixel per lane. Two kernels share
+// the list walks (forward_walk, gradient_walk):
+//   tile kernel    one CTA per (scene, 16x16 tile[, triangle block]), 8 warps,
+//                  warp w on block w; long lists binned in chunks
+//   region kernel  one CTA per (scene, 2x2 tiles) for lists within one chunk;
+//                  warps take the region's 32 blocks from a shared counter
+// Triangles are binned in order (build_list, build_region_list) and every
+// kept entry carries a one-byte code per warp block, decided once at binning
+// time from the block's rectangle against the triangle's box and edge lines:
 //   kBlkSkip    no pixel of the block can contribute (outside the box, or
 //               every pixel more than the triangle's `rej` outside an edge)
 //   kBlkBox     the block straddles the box: test each pixel against it
@@ -212,7 +218,7 @@ __global__ void __launch_bounds__(kSetupThreads) dr_setup_kernel(
 constexpr int kBlkSkip = 1, kBlkBox = 2, kBlkInside = 4, kCandShift = 3;
 struct Smem {
   TriRec rec[kChunk];
-  unsigned char bcode[kChunk][8];
+  unsigned char bcode[kChunk][kBlocksPerTile];
   int kidx[kChunk];
   float acc[kChunk][kParams];
   int warp_count[kWarps];
