@@ -432,6 +432,68 @@ dr_status dr_loss_backward_sharded(dr_ctx* ctx, const float* params, const float
                          (cudaStream_t)stream);
 }
 
+dr_status dr_triangle_block_forward(dr_ctx* ctx, const float* params, const float* background,
+                                    int bg_per_scene, int B, int T, int H, int W, float sigma,
+                                    int n_blocks, int block, float* state, dr_stream_t stream) {
+  dr_status st = check_common(ctx, params, B, T, H, W, sigma, DR_LAYOUT_BHWC);
+  if (st) return st;
+  if (n_blocks < 1 || n_blocks > 65535 || block < 0 || block >= n_blocks)
+    return fail(DR_INVALID_ARGUMENT, "block %d of %d is out of range", block, n_blocks);
+  if (B > 0 && !state) return fail(DR_INVALID_ARGUMENT, "null state pointer");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  if (B == 0) return DR_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  RasterArgs a;
+  st = prepare(ctx, params, background, bg_per_scene, B, T, H, W, sigma, DR_LAYOUT_BHWC, 1, a, s);
+  if (st) return st;
+  const int n_tiles = a.tiles_x * ((H + kTileSide - 1) / kTileSide);
+  DR_CUDA(launch_triangle_block(0, kModeLoss, a, n_tiles, n_blocks, block, (float4*)state, nullptr,
+                                s),
+          "triangle-block forward");
+  return DR_OK;
+}
+
+dr_status dr_triangle_block_backward(dr_ctx* ctx, const float* params, const float* background,
+                                     int bg_per_scene, int B, int T, int H, int W, float sigma,
+                                     int n_blocks, int block, const float* state,
+                                     const float* other, int layout, int grad_input, float* grads,
+                                     float* losses, float* image, dr_stream_t stream) {
+  dr_status st = check_common(ctx, params, B, T, H, W, sigma, layout);
+  if (st) return st;
+  if (n_blocks < 1 || n_blocks > 65535 || block < 0 || block >= n_blocks)
+    return fail(DR_INVALID_ARGUMENT, "block %d of %d is out of range", block, n_blocks);
+  if (grad_input != 0 && grad_input != 1)
+    return fail(DR_INVALID_ARGUMENT, "grad_input must be 0 (target) or 1 (image gradient)");
+  if (B > 0 && (!state || !other || (T > 0 && !grads)))
+    return fail(DR_INVALID_ARGUMENT, "null state, target/gradient or grads pointer");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  if (B == 0) return DR_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (T > 0)
+    DR_CUDA(cudaMemsetAsync(grads, 0, sizeof(float) * (size_t)B * T * kParams, s), "zero grads");
+  RasterArgs a;
+  st = prepare(ctx, params, background, bg_per_scene, B, T, H, W, sigma, layout, 1, a, s);
+  if (st) return st;
+  const int n_tiles = a.tiles_x * ((H + kTileSide - 1) / kTileSide);
+  const int mode = grad_input ? kModeGrad : kModeLoss;
+  a.other = other;
+  a.grads = grads;
+  a.image = image;
+  a.losses = losses;
+  if (mode == kModeLoss) {
+    st = loss_scratch(ctx, a, n_tiles);
+    if (st) return st;
+  }
+  st = ensure(ctx, ctx->split, raster_split_bytes(B, 1, H, W), false);
+  if (st) return st;
+  DR_CUDA(launch_triangle_block(1, mode, a, n_tiles, n_blocks, block,
+                                (float4*)const_cast<float*>(state), (float4*)ctx->split.ptr, s),
+          "triangle-block backward");
+  return DR_OK;
+}
+
 dr_status dr_mse_loss(dr_ctx* ctx, const float* images, const float* targets, int B,
                       int64_t n_per_image, float* losses, dr_stream_t stream) {
   if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");

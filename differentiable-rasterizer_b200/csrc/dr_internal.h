@@ -40,7 +40,10 @@ struct RasterArgs {
   double n_values;            // H*W*3
   const int* skip_flag;       // optional: nonzero -> the kernel does nothing
   int split_k;                // triangle blocks of a split launch (else 0)
-  float4* split;              // split state: 4 float4 per (scene, block, pixel)
+  int split_base;             // first block of this launch (grid z adds to it)
+  int split_own;              // >= 0: only this block's backward state is kept
+  float4* split_fwd;          // per (block, scene, pixel): 2 float4 of forward state
+  float4* split_bwd;          // per (block or 1, scene, pixel): 2 float4 from the combine
 };
 
 struct AdamArgs {
@@ -97,6 +100,14 @@ inline size_t raster_split_bytes(int B, int k, int H, int W) {
 // step 1).
 cudaError_t launch_raster_split(int mode, const RasterArgs& a, int n_tiles, int k, float4* split,
                                 cudaStream_t s);
+// One GPU's share of a scene batch sharded by triangle blocks: phase 0 runs
+// block `block`'s forward over all pixels into its slice of fwd_state
+// (n_blocks x B x H x W x 32 bytes); phase 1, with every slice present, runs
+// the combine (final colour, loss) and the block's gradient pass, using
+// bwd_state (B x H x W x 32 bytes) as scratch.
+cudaError_t launch_triangle_block(int phase, int mode, const RasterArgs& a, int n_tiles,
+                                  int n_blocks, int block, float4* fwd_state, float4* bwd_state,
+                                  cudaStream_t s);
 // Per-image MSE scratch: B * mse_partials_per_image(n) doubles and B counters
 // (zero between launches; the kernel leaves them zero).
 size_t mse_partials_per_image(long long n);

@@ -1163,13 +1163,29 @@ __device__ __forceinline__ void scene_loss(const RasterArgs& a, int b, int slot,
   }
 }
 
-// Split state of one pixel of one triangle block: [c0 c1 c2 m] [e z0 zn -]
-// written by the block's forward (composite over black, running product),
-// then [g0 g1 g2 -] [d0 d1 d2 -] written by the combine (the gradient reaching
-// the block, the canvas entering it).
-__device__ __forceinline__ float4* split_pixel(const RasterArgs& a, int b, int kblk, int px,
-                                               int py) {
-  return a.split + ((size_t)(b * a.split_k + kblk) * a.H * a.W + (size_t)py * a.W + px) * 4;
+// Split state, block-major so that one block's slice is contiguous (ranks of
+// a triangle-sharded scene all-gather their slices):
+//   forward  [c0 c1 c2 m] [e z0 zn -] per (block, scene, pixel): the block's
+//            composite over black and running product (its forward pass);
+//   backward [g0 g1 g2 -] [d0 d1 d2 a] per (block, scene, pixel): from the
+//            combine, the gradient reaching the block, the canvas entering it
+//            and the block's map factor a. With split_own >= 0 only that
+//            block's backward state is kept (slice 0).
+__device__ __forceinline__ float4* split_fwd_pixel(const RasterArgs& a, int k, int b, int px,
+                                                   int py) {
+  return a.split_fwd + (((size_t)k * a.B + b) * a.H * a.W + (size_t)py * a.W + px) * 2;
+}
+__device__ __forceinline__ float4* split_bwd_pixel(const RasterArgs& a, int k, int b, int px,
+                                                   int py) {
+  const int slot = a.split_own >= 0 ? 0 : k;
+  return a.split_bwd + (((size_t)slot * a.B + b) * a.H * a.W + (size_t)py * a.W + px) * 2;
+}
+
+// Factor a of a block's map x -> a x + c from its forward state: NaN after a
+// NaN layer, 0 after an opaque one, else the renormalised running product.
+__device__ __forceinline__ float block_factor(const float4& s0, const float4& s1) {
+  const int e = __float_as_int(s1.x), z0 = __float_as_int(s1.y), zn = __float_as_int(s1.z);
+  return zn >= 0 ? __int_as_float(0x7fc00000) : (z0 >= 0 ? 0.0f : ldexpf(s0.w, -64 * e));
 }
 
 // Tile kernel: one CTA per (scene, 16x16 tile[, triangle block]), warp w on
@@ -1195,11 +1211,12 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   Consts K;
   K.sigma_eff = a.sigma_eff;
   K.inv_sigma = a.inv_sigma;
-  // Triangles [t0, t1): all of them, or this CTA's block of a split launch.
+  // Triangles [t0, t1): all of them, or block kb of a split launch.
+  const int kb = a.split_base + (int)blockIdx.z;
   int t0 = 0, t1 = a.T;
   if (kSplit) {
     const int per = (a.T + a.split_k - 1) / a.split_k;
-    t0 = min(a.T, (int)blockIdx.z * per);
+    t0 = min(a.T, kb * per);
     t1 = min(a.T, t0 + per);
   }
   const int n_chunks = (t1 - t0 + kChunk - 1) / kChunk;
@@ -1219,7 +1236,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     }
     if (Mode == kModeSplitFwd) {
       if (active) {
-        float4* sp = split_pixel(a, b, blockIdx.z, px, py);
+        float4* sp = split_fwd_pixel(a, kb, b, px, py);
         sp[0] = make_float4(c0, c1, c2, P.m);
         sp[1] = make_float4(__int_as_float(P.e), __int_as_float(P.z0), __int_as_float(P.zn), 0.f);
       }
@@ -1241,8 +1258,9 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     // gradient reaching the block and the canvas entering it.
     r0 = r1 = r2 = 0.0f;
     if (active) {
-      const float4* sp = split_pixel(a, b, blockIdx.z, px, py);
-      const float4 s0 = sp[0], s1 = sp[1], s2 = sp[2], s3 = sp[3];
+      const float4* sf = split_fwd_pixel(a, kb, b, px, py);
+      const float4* sb = split_bwd_pixel(a, kb, b, px, py);
+      const float4 s0 = sf[0], s1 = sf[1], s2 = sb[0], s3 = sb[1];
       P.m = s0.w;
       P.e = __float_as_int(s1.x);
       P.z0 = __float_as_int(s1.y);
@@ -1283,8 +1301,6 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
 // canvas entering block k is the composition of the maps below applied to the
 // background; the final colour is the composition of all. The gradient
 // reaching block k is G times the product of a_j over the blocks above.
-constexpr int kMaxSplit = 8;  // automatic splits use at most this many blocks
-
 template <int Mode>
 __global__ void __launch_bounds__(kThreads) dr_split_combine_kernel(RasterArgs a) {
   __shared__ double loss_part[kWarps];
@@ -1301,48 +1317,29 @@ __global__ void __launch_bounds__(kThreads) dr_split_combine_kernel(RasterArgs a
   if (active) {
     float d0, d1, d2;
     scene_background(a, b, d0, d1, d2);
-    // Block maps in registers for up to kMaxSplit blocks (all loads issued
-    // together); a forced larger split re-reads them.
-    float ak[kMaxSplit];
+    // Block factors are recomputed from the forward state on the way back
+    // (L2-resident loads) rather than held in a dynamically indexed array.
     const int kk = a.split_k;
-#pragma unroll
-    for (int k = 0; k < kMaxSplit; ++k) {
-      if (k >= kk) break;
-      float4* sp = split_pixel(a, b, k, px, py);
-      const float4 s0 = __ldcg(sp), s1 = __ldcg(sp + 1);
-      const int e = __float_as_int(s1.x), z0 = __float_as_int(s1.y), zn = __float_as_int(s1.z);
-      ak[k] = zn >= 0 ? __int_as_float(0x7fc00000) : (z0 >= 0 ? 0.0f : ldexpf(s0.w, -64 * e));
-      sp[3] = make_float4(d0, d1, d2, ak[k]);
-      d0 = __fadd_rn(__fmul_rn(ak[k], d0), s0.x);
-      d1 = __fadd_rn(__fmul_rn(ak[k], d1), s0.y);
-      d2 = __fadd_rn(__fmul_rn(ak[k], d2), s0.z);
-    }
-    for (int k = kMaxSplit; k < kk; ++k) {
-      float4* sp = split_pixel(a, b, k, px, py);
-      const float4 s0 = sp[0], s1 = sp[1];
-      const int e = __float_as_int(s1.x), z0 = __float_as_int(s1.y), zn = __float_as_int(s1.z);
-      const float akk = zn >= 0 ? __int_as_float(0x7fc00000)
-                                : (z0 >= 0 ? 0.0f : ldexpf(s0.w, -64 * e));
-      sp[3] = make_float4(d0, d1, d2, akk);
-      d0 = __fadd_rn(__fmul_rn(akk, d0), s0.x);
-      d1 = __fadd_rn(__fmul_rn(akk, d1), s0.y);
-      d2 = __fadd_rn(__fmul_rn(akk, d2), s0.z);
+    for (int k = 0; k < kk; ++k) {
+      const float4* sf = split_fwd_pixel(a, k, b, px, py);
+      const float4 s0 = __ldcg(sf), s1 = __ldcg(sf + 1);
+      const float f = block_factor(s0, s1);
+      if (a.split_own < 0 || k == a.split_own)
+        split_bwd_pixel(a, k, b, px, py)[1] = make_float4(d0, d1, d2, f);
+      d0 = __fadd_rn(__fmul_rn(f, d0), s0.x);
+      d1 = __fadd_rn(__fmul_rn(f, d1), s0.y);
+      d2 = __fadd_rn(__fmul_rn(f, d2), s0.z);
     }
     if (a.image) store_pixel(a, b, px, py, d0, d1, d2);
     float G0, G1, G2;
     top_gradient<Mode>(a, b, px, py, true, d0, d1, d2, G0, G1, G2, sq);
     float above = 1.0f;
-    for (int k = kk - 1; k >= kMaxSplit; --k) {
-      float4* sp = split_pixel(a, b, k, px, py);
-      sp[2] = make_float4(__fmul_rn(G0, above), __fmul_rn(G1, above), __fmul_rn(G2, above), 0.f);
-      above = __fmul_rn(above, sp[3].w);
-    }
-#pragma unroll
-    for (int k = kMaxSplit - 1; k >= 0; --k) {
-      if (k >= kk) continue;
-      float4* sp = split_pixel(a, b, k, px, py);
-      sp[2] = make_float4(__fmul_rn(G0, above), __fmul_rn(G1, above), __fmul_rn(G2, above), 0.f);
-      above = __fmul_rn(above, ak[k]);
+    for (int k = kk - 1; k >= 0; --k) {
+      if (a.split_own < 0 || k == a.split_own)
+        split_bwd_pixel(a, k, b, px, py)[0] =
+            make_float4(__fmul_rn(G0, above), __fmul_rn(G1, above), __fmul_rn(G2, above), 0.f);
+      const float4* sf = split_fwd_pixel(a, k, b, px, py);
+      above = __fmul_rn(above, block_factor(__ldcg(sf), __ldcg(sf + 1)));
     }
   }
   if (Mode == kModeLoss) {
@@ -1716,11 +1713,55 @@ cudaError_t launch_raster_split(int mode, const RasterArgs& args, int n_tiles, i
   RasterArgs a = args;
   a.tile_rows = n_tiles / a.tiles_x;
   a.split_k = k;
-  a.split = split;
+  a.split_base = 0;
+  a.split_own = -1;
+  a.split_fwd = split;
+  a.split_bwd = split + (size_t)k * a.B * a.H * a.W * 2;
   switch (a.precision) {
     case kPrecRef: return launch_split_prec<kPrecRef>(mode, a, n_tiles, s);
     case kPrecStrict: return launch_split_prec<kPrecStrict>(mode, a, n_tiles, s);
     case kPrecFast: return launch_split_prec<kPrecFast>(mode, a, n_tiles, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <int kPrec>
+static cudaError_t launch_block_prec(int phase, int mode, const RasterArgs& a, int n_tiles,
+                                     cudaStream_t s) {
+  dim3 grid3(n_tiles, a.B, 1), grid2(n_tiles, a.B);
+  if (phase == 0) {
+    dr_raster_kernel<kModeSplitFwd, kPrec><<<grid3, kThreads, sizeof(Smem), s>>>(a);
+    return cudaGetLastError();
+  }
+  if (mode == kModeLoss) dr_split_combine_kernel<kModeLoss><<<grid2, kThreads, 0, s>>>(a);
+  else dr_split_combine_kernel<kModeGrad><<<grid2, kThreads, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  RasterArgs f = a;
+  f.image = nullptr;
+  dr_raster_kernel<kModeSplitBwd, kPrec><<<grid3, kThreads, sizeof(Smem), s>>>(f);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_triangle_block(int phase, int mode, const RasterArgs& args, int n_tiles,
+                                  int n_blocks, int block, float4* fwd_state, float4* bwd_state,
+                                  cudaStream_t s) {
+  if (args.B == 0 || n_tiles == 0) return cudaSuccess;
+  if (args.tiles_x <= 0 || n_blocks < 1 || block < 0 || block >= n_blocks || !fwd_state ||
+      (phase == 1 && (!bwd_state || (mode != kModeLoss && mode != kModeGrad))) ||
+      args.tile_row0 != 0 || args.tile_row_step != 1)
+    return cudaErrorInvalidValue;
+  RasterArgs a = args;
+  a.tile_rows = n_tiles / a.tiles_x;
+  a.split_k = n_blocks;
+  a.split_base = block;
+  a.split_own = block;
+  a.split_fwd = fwd_state;
+  a.split_bwd = bwd_state;
+  switch (a.precision) {
+    case kPrecRef: return launch_block_prec<kPrecRef>(phase, mode, a, n_tiles, s);
+    case kPrecStrict: return launch_block_prec<kPrecStrict>(phase, mode, a, n_tiles, s);
+    case kPrecFast: return launch_block_prec<kPrecFast>(phase, mode, a, n_tiles, s);
   }
   return cudaErrorInvalidValue;
 }

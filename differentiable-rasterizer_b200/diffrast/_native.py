@@ -82,6 +82,10 @@ SIGNATURES = {
     "dr_grad_backward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P]),
     "dr_loss_backward_sharded": (
         _I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _I, _I, _P, _P, _P]),
+    "dr_triangle_block_forward": (
+        _I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _I, _P, _P]),
+    "dr_triangle_block_backward": (
+        _I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "dr_mse_loss": (_I, [_P, _P, _P, _I, ctypes.c_int64, _P, _P]),
     "dr_adam_step": (
         _I, [_P, _P, _P, _P, _P, ctypes.c_int64, _F, _F, _F, ctypes.c_uint32, _F, _F, _F, _I, _P]),
@@ -411,6 +415,65 @@ def loss_backward_sharded(params: torch.Tensor, targets: torch.Tensor, sigma: fl
                                          sigma, _ptr(t), layout, shard, n_shards, _ptr(grads),
                                          _ptr(sums), ctypes.c_void_p(s)))
     return sums, grads
+
+
+TRIANGLE_BLOCK_STATE_FLOATS = 8  # DR_TRIANGLE_BLOCK_STATE_BYTES / 4
+
+
+def triangle_block_state(params: torch.Tensor, height: int, width: int,
+                         n_blocks: int) -> torch.Tensor:
+    """A (n_blocks, B, H, W, 8) f32 buffer for the triangle-block calls."""
+    dev = _resolve_device(params.device)
+    B = params.shape[0]
+    return torch.empty((n_blocks, B, height, width, TRIANGLE_BLOCK_STATE_FLOATS),
+                       dtype=torch.float32, device=dev)
+
+
+def triangle_block_forward(params: torch.Tensor, height: int, width: int, sigma: float,
+                           n_blocks: int, block: int, state: torch.Tensor,
+                           background=(0.0, 0.0, 0.0)) -> None:
+    """dr_triangle_block_forward into state[block] (see triangle_block_state)."""
+    sigma = _check_sigma(sigma)
+    dev = _resolve_device(params.device)
+    p = _as_cuda_f32(params, dev)
+    B, T = p.shape[0], p.shape[1]
+    if tuple(state.shape) != (n_blocks, B, height, width, TRIANGLE_BLOCK_STATE_FLOATS) or \
+            not state.is_contiguous() or state.dtype != torch.float32 or state.device != dev:
+        raise ValueError("state must come from triangle_block_state(params, H, W, n_blocks)")
+    bg, per = _bg_host(background, B)
+    s = _stream(dev)
+    check(lib().dr_triangle_block_forward(context(dev, s), _ptr(p), _ptr(bg), per, B, T, height,
+                                          width, sigma, n_blocks, block, _ptr(state),
+                                          ctypes.c_void_p(s)))
+
+
+def triangle_block_backward(params: torch.Tensor, state: torch.Tensor, other: torch.Tensor,
+                            sigma: float, n_blocks: int, block: int, background=(0.0, 0.0, 0.0),
+                            layout: int = LAYOUT_BHWC, grad_input: bool = False,
+                            want_image: bool = False):
+    """dr_triangle_block_backward with every slice of `state` filled. Returns
+    (losses (B,) or None, grads (B, T, 10) nonzero on block `block`[, image])."""
+    sigma = _check_sigma(sigma)
+    dev = _resolve_device(params.device)
+    p = _as_cuda_f32(params, dev)
+    o = _as_cuda_f32(other, dev)
+    B, T = p.shape[0], p.shape[1]
+    H, W = (o.shape[2], o.shape[3]) if layout == LAYOUT_BCHW else (o.shape[1], o.shape[2])
+    if tuple(state.shape) != (n_blocks, B, H, W, TRIANGLE_BLOCK_STATE_FLOATS) or \
+            not state.is_contiguous() or state.dtype != torch.float32 or state.device != dev:
+        raise ValueError("state must come from triangle_block_state(params, H, W, n_blocks)")
+    grads = torch.empty((B, T, N_PARAMS), dtype=torch.float32, device=dev)
+    losses = None if grad_input else torch.empty((B,), dtype=torch.float32, device=dev)
+    image = torch.empty_like(o) if want_image else None
+    bg, per = _bg_host(background, B)
+    s = _stream(dev)
+    check(lib().dr_triangle_block_backward(context(dev, s), _ptr(p), _ptr(bg), per, B, T, H, W,
+                                           sigma, n_blocks, block, _ptr(state), _ptr(o), layout,
+                                           1 if grad_input else 0, _ptr(grads), _ptr(losses),
+                                           _ptr(image), ctypes.c_void_p(s)))
+    if want_image:
+        return losses, grads, image
+    return losses, grads
 
 
 def mse_loss(images: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:

@@ -162,6 +162,36 @@ DR_API dr_status dr_loss_backward_sharded(dr_ctx* ctx, const float* params, cons
                                    const float* targets, int layout, int shard, int n_shards,
                                    float* grads, double* loss_sums, dr_stream_t stream);
 
+/* One scene batch sharded by triangle blocks across devices (or run block by
+ * block on one): the triangles are cut into n_blocks consecutive blocks of
+ * ceil(T / n_blocks), and each caller owns block `block`. No reference
+ * counterpart: the reference has no multi-device path.
+ *
+ * dr_triangle_block_forward composites the block over black for every pixel.
+ * It writes the block's running product into slice `block` of `state`, a device
+ * buffer of n_blocks * B * H * W * DR_TRIANGLE_BLOCK_STATE_BYTES bytes, block-major
+ * (each slice contiguous, so ranks can all-gather their slices).
+ *
+ * dr_triangle_block_backward needs every slice of `state`. It combines the
+ * blocks' per-pixel maps into the final image (optional `image`, layout as
+ * `other`) and the per-scene loss (`losses`, when grad_input == 0). It then runs
+ * block `block`'s gradient pass: `grads` (B, T, 10) is overwritten, nonzero only
+ * on the block's triangles. `other` is the target (grad_input == 0, MSE as
+ * dr_loss_backward) or the upstream image gradient (grad_input == 1, as
+ * dr_grad_backward). The sum of `grads` over all blocks equals dr_loss_backward
+ * to rounding. */
+#define DR_TRIANGLE_BLOCK_STATE_BYTES 32
+DR_API dr_status dr_triangle_block_forward(dr_ctx* ctx, const float* params,
+                                           const float* background, int bg_per_scene, int B,
+                                           int T, int H, int W, float sigma, int n_blocks,
+                                           int block, float* state, dr_stream_t stream);
+DR_API dr_status dr_triangle_block_backward(dr_ctx* ctx, const float* params,
+                                            const float* background, int bg_per_scene, int B,
+                                            int T, int H, int W, float sigma, int n_blocks,
+                                            int block, const float* state, const float* other,
+                                            int layout, int grad_input, float* grads,
+                                            float* losses, float* image, dr_stream_t stream);
+
 /* Per-image MSE of two (B, n) arrays with an f64 sum.
  * Replaces GpuRasterizer::encode_loss / loss_batch.wgsl (diffrast-gpu/src/lib.rs:1004-1031)
  * and Canvas::mse (crates/diffrast/src/canvas.rs:45-59). */

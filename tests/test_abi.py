@@ -30,7 +30,8 @@ def declared_symbols():
 def test_header_declares_the_entry_points():
     names = declared_symbols()
     for required in ("dr_ctx_create", "dr_render", "dr_loss_backward", "dr_grad_backward",
-                     "dr_mse_loss", "dr_adam_step", "dr_fit", "dr_loss_backward_sharded"):
+                     "dr_mse_loss", "dr_adam_step", "dr_fit", "dr_loss_backward_sharded",
+                     "dr_triangle_block_forward", "dr_triangle_block_backward"):
         assert required in names
 
 
@@ -85,3 +86,7 @@ def test_argument_errors_need_no_device():
         _native.INVALID_ARGUMENT
     assert L.dr_adam_step(None, None, None, None, None, 1, 0.1, 0.1, 0.1, 1, 0.9, 0.999, 1e-8, 1,
                           None) == _native.INVALID_ARGUMENT
+    assert L.dr_triangle_block_forward(None, None, None, 0, 1, 1, 8, 8, 0.01, 2, 0, None,
+                                       None) == _native.INVALID_ARGUMENT
+    assert L.dr_triangle_block_backward(None, None, None, 0, 1, 1, 8, 8, 0.01, 2, 1, None, None, 0,
+                                        0, None, None, None, None) == _native.INVALID_ARGUMENT

@@ -172,3 +172,194 @@ def test_two_gpu_sharded_step_matches_one_gpu():
         _native.adam_step(p, m, v, g, t)
     np.testing.assert_allclose(res[0][0], losses.cpu().numpy(), rtol=1e-5)
     np.testing.assert_allclose(np.array(res[0][1]), p.cpu().numpy(), rtol=1e-4, atol=1e-6)
+
+
+# ---- triangle-block sharding (TriangleShardedStep) --------------------------
+
+
+def test_triangle_blocks_cover_every_triangle_once():
+    from diffrast.sharded import triangle_block
+
+    for T in (0, 1, 5, 63, 64, 150, 1000):
+        for n in (1, 2, 3, 4, 8):
+            got = [t for k in range(n) for t in range(*triangle_block(T, n, k))]
+            assert got == list(range(T)), (T, n)
+    with pytest.raises(ValueError):
+        triangle_block(10, 2, 2)
+
+
+def _gloo_block_worker(rank, world, port, out):
+    import sys
+
+    for p in (REPO, PKG):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    from diffrast import _native, sharded
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+
+    def fake_state(params, h, w, n_blocks):
+        return torch.zeros(n_blocks, params.shape[0], h, w, 8)
+
+    def fake_forward(params, h, w, sigma, n_blocks, block, state, background=(0.0, 0.0, 0.0)):
+        # Only the own slice is written, like the kernel.
+        state[block] = float(block + 1)
+
+    def fake_backward(params, state, other, sigma, n_blocks, block, background=(0.0, 0.0, 0.0)):
+        # The loss depends on every block's slice; the gradient only on the own block.
+        loss = torch.tensor([float(state.sum())])
+        g = torch.zeros_like(params)
+        t0, t1 = sharded.triangle_block(params.shape[1], n_blocks, block)
+        g[:, t0:t1] = float(block + 1)
+        return loss, g
+
+    def fake_adam(params, m, v, grads, step, *lrs):
+        params -= grads
+
+    _native.triangle_block_state = fake_state
+    _native.triangle_block_forward = fake_forward
+    _native.triangle_block_backward = fake_backward
+    _native.adam_step = fake_adam
+    step = sharded.TriangleShardedStep(torch.zeros(1, 5, 10))
+    losses = step.step(torch.zeros(1, 2, 2, 3), 0.01)
+    full = step.gather_params()
+    out[rank] = (losses.tolist(), step.params.reshape(-1).tolist(), full.reshape(-1).tolist())
+    dist.destroy_process_group()
+
+
+def test_triangle_block_plumbing_on_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_gloo_block_worker, args=(r, 2, port, out)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(120)
+            assert p.exitcode == 0
+        res = dict(out)
+    # Both ranks combine the same gathered state: (1 + 2) * 2*2*8 per slice.
+    assert res[0][0] == res[1][0] == [float((1 + 2) * 2 * 2 * 8)]
+    own0 = np.array(res[0][1]).reshape(5, 10)
+    own1 = np.array(res[1][1]).reshape(5, 10)
+    assert np.all(own0[:3] == -1.0) and np.all(own0[3:] == 0.0)  # blocks [0,3) and [3,5)
+    assert np.all(own1[:3] == 0.0) and np.all(own1[3:] == -2.0)
+    full = np.array(res[0][2]).reshape(5, 10)
+    assert np.array_equal(full, np.array(res[1][2]).reshape(5, 10))
+    assert np.all(full[:3] == -1.0) and np.all(full[3:] == -2.0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n_blocks", [1, 2, 3, 4])
+def test_triangle_blocks_emulated_on_one_gpu_match_the_oracle(oracle, n_blocks):
+    # Every rank's calls run here in turn on one GPU: forward of each block
+    # into its slice of the state, then the backward of each block. Every
+    # block's call gives the same image and losses; the blocks' gradients sum
+    # to the whole scene's. Opaque and NaN-alpha layers, per-scene backgrounds,
+    # a ragged canvas.
+    from diffrast import _native
+    from diffrast.scenes import config5_params, uniform_scenes
+
+    from conftest import assert_images_close
+
+    p = np.concatenate([uniform_scenes(2, 96, 91), config5_params(1, 96, 5201)], axis=0)
+    p[0, 10, 9] = 1.0
+    p[1, 70, 9] = np.nan
+    bg = np.random.default_rng(8).uniform(0, 1, (3, 3)).astype(np.float32)
+    H, W, sigma = 37, 45, 0.004
+    target = oracle.render_batch(uniform_scenes(3, 60, 92), H, W, sigma, bg)
+    ref_l, ref_g, ref_img = oracle.backward_batch(p, target, sigma, bg, want_images=True)
+    pc, tc = torch.from_numpy(p).cuda(), torch.from_numpy(target).cuda()
+    state = _native.triangle_block_state(pc, H, W, n_blocks)
+    for k in range(n_blocks):
+        _native.triangle_block_forward(pc, H, W, sigma, n_blocks, k, state, bg)
+    total = np.zeros_like(ref_g)
+    first = None
+    for k in range(n_blocks):
+        losses, g, img = _native.triangle_block_backward(pc, state, tc, sigma, n_blocks, k, bg,
+                                                         want_image=True)
+        losses, g, img = losses.cpu().numpy(), g.cpu().numpy(), img.cpu().numpy()
+        if first is None:
+            first = (losses, img)
+        else:  # the combine is the same computation on every rank
+            assert np.array_equal(losses, first[0]) and np.array_equal(img, first[1])
+        t0, t1 = (lambda per: (min(96, k * per), min(96, k * per + per)))(-(-96 // n_blocks))
+        assert not np.any(g[:, :t0]) and not np.any(g[:, t1:])
+        total += g
+    assert_images_close(first[1], ref_img, "triangle-block image")
+    np.testing.assert_allclose(first[0], ref_l, rtol=1e-5, atol=1e-9)
+    assert_grads_close(total, ref_g, "triangle-block grads")
+    # Upstream-gradient mode.
+    g_in = np.random.default_rng(9).normal(0, 1e-4, size=target.shape).astype(np.float32)
+    _, ref_gg = oracle.backward_batch(p, g_in, sigma, bg, mode=oracle.MODE_DIRECT_GRAD)
+    gg = sum(_native.triangle_block_backward(pc, state, torch.from_numpy(g_in).cuda(), sigma,
+                                             n_blocks, k, bg, grad_input=True)[1].cpu().numpy()
+             for k in range(n_blocks))
+    assert_grads_close(gg, ref_gg, "triangle-block grad-input")
+
+
+def _nccl_block_worker(rank, world, port, out):
+    import sys
+
+    for p in (REPO, PKG):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+
+    import torch.distributed as dist
+
+    from diffrast import _native, sharded
+    from diffrast.scenes import config1_target_scene, seed_scene_geometry
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    target = _native.render(torch.from_numpy(config1_target_scene(256, 0)).cuda(), 96, 96, 0.0015)
+    p = torch.from_numpy(seed_scene_geometry(256, 1)).cuda()
+    p[:, :, 6:9] = 0.5
+    step = sharded.TriangleShardedStep(p)
+    hist = [step.step(target, 0.0015).cpu().tolist() for _ in range(3)]
+    full = step.gather_params()
+    torch.cuda.synchronize()
+    out[rank] = (hist, full.cpu().numpy().tolist())
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_two_gpu_triangle_sharded_step_matches_one_gpu():
+    from diffrast import _native
+    from diffrast.scenes import config1_target_scene, seed_scene_geometry
+
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_nccl_block_worker, args=(r, 2, port, out)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(300)
+            assert p.exitcode == 0
+        res = dict(out)
+    assert res[0] == res[1]  # same losses and assembled parameters on both ranks
+    target = _native.render(torch.from_numpy(config1_target_scene(256, 0)).cuda(), 96, 96, 0.0015)
+    p = torch.from_numpy(seed_scene_geometry(256, 1)).cuda()
+    p[:, :, 6:9] = 0.5
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    hist = []
+    for t in range(1, 4):
+        losses, g = _native.loss_backward(p, target, 0.0015)
+        hist.append(losses.cpu().tolist())
+        _native.adam_step(p, m, v, g, t)
+    np.testing.assert_allclose(np.array(res[0][0]), np.array(hist), rtol=1e-5)
+    np.testing.assert_allclose(np.array(res[0][1]), p.cpu().numpy(), rtol=1e-4, atol=1e-6)
