@@ -138,11 +138,36 @@ def _nccl_worker(rank, world, port, out):
     target = _native.render(torch.from_numpy(config4_params(1024, 4001)).cuda(), 512, 512,
                             0.0015)
     step = sharded.ShardedSceneStep(p)
-    for _ in range(3):
-        losses = step.step(target, 0.0015)
+    _, g = step.loss_and_grads(target, 0.0015)
+    hist = [step.step(target, 0.0015).cpu().tolist() for _ in range(3)]
     torch.cuda.synchronize()
-    out[rank] = (losses.cpu().tolist(), step.params.cpu().numpy().tolist())
+    out[rank] = (hist, step.params.cpu().numpy().tolist(), g.cpu().numpy().tolist())
     dist.destroy_process_group()
+
+
+def _check_against_one_gpu(res, p, target):
+    """Three single-GPU steps of loss_backward + Adam from the same start.
+
+    The first gradient matches to the parity tolerance. Adam normalises each
+    update, so a gradient that differs by rounding near zero can move its
+    parameter by up to one learning rate more or less; the parameters after
+    three steps must match closely except on such rare elements, and those stay
+    within the step bound 2 x lr x steps."""
+    from diffrast import _native
+
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    hist = []
+    for t in range(1, 4):
+        losses, g = _native.loss_backward(p, target, 0.0015)
+        if t == 1:
+            assert_grads_close(np.array(res[2], np.float32), g.cpu().numpy(), "first gradient")
+        hist.append(losses.cpu().tolist())
+        _native.adam_step(p, m, v, g, t)
+    np.testing.assert_allclose(np.array(res[0]), np.array(hist), rtol=1e-5)
+    got, ref = np.array(res[1], np.float32), p.cpu().numpy()
+    off = np.abs(got - ref) > 1e-6 + 1e-4 * np.abs(ref)
+    assert off.mean() < 1e-3, f"{off.sum()} of {off.size} parameters differ"
+    assert np.all(np.abs(got - ref) <= 2 * 0.02 * 3 + 1e-6)
 
 
 @pytest.mark.gpu
@@ -166,12 +191,7 @@ def test_two_gpu_sharded_step_matches_one_gpu():
     assert res[0] == res[1]  # replicated parameters stay identical
     p = torch.from_numpy(config4_params(1024, 4000)).cuda()
     target = _native.render(torch.from_numpy(config4_params(1024, 4001)).cuda(), 512, 512, 0.0015)
-    m, v = torch.zeros_like(p), torch.zeros_like(p)
-    for t in range(1, 4):
-        losses, g = _native.loss_backward(p, target, 0.0015)
-        _native.adam_step(p, m, v, g, t)
-    np.testing.assert_allclose(res[0][0], losses.cpu().numpy(), rtol=1e-5)
-    np.testing.assert_allclose(np.array(res[0][1]), p.cpu().numpy(), rtol=1e-4, atol=1e-6)
+    _check_against_one_gpu(res[0], p, target)
 
 
 # ---- triangle-block sharding (TriangleShardedStep) --------------------------
@@ -323,13 +343,15 @@ def _nccl_block_worker(rank, world, port, out):
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     target = _native.render(torch.from_numpy(config1_target_scene(256, 0)).cuda(), 96, 96, 0.0015)
-    p = torch.from_numpy(seed_scene_geometry(256, 1)).cuda()
+    p = torch.from_numpy(seed_scene_geometry(256, 1))[None].cuda()
     p[:, :, 6:9] = 0.5
     step = sharded.TriangleShardedStep(p)
+    _, g = step.loss_and_grads(target, 0.0015)
+    dist.all_reduce(g)  # the blocks' gradients are disjoint
     hist = [step.step(target, 0.0015).cpu().tolist() for _ in range(3)]
     full = step.gather_params()
     torch.cuda.synchronize()
-    out[rank] = (hist, full.cpu().numpy().tolist())
+    out[rank] = (hist, full.cpu().numpy().tolist(), g.cpu().numpy().tolist())
     dist.destroy_process_group()
 
 
@@ -353,13 +375,6 @@ def test_two_gpu_triangle_sharded_step_matches_one_gpu():
         res = dict(out)
     assert res[0] == res[1]  # same losses and assembled parameters on both ranks
     target = _native.render(torch.from_numpy(config1_target_scene(256, 0)).cuda(), 96, 96, 0.0015)
-    p = torch.from_numpy(seed_scene_geometry(256, 1)).cuda()
+    p = torch.from_numpy(seed_scene_geometry(256, 1))[None].cuda()
     p[:, :, 6:9] = 0.5
-    m, v = torch.zeros_like(p), torch.zeros_like(p)
-    hist = []
-    for t in range(1, 4):
-        losses, g = _native.loss_backward(p, target, 0.0015)
-        hist.append(losses.cpu().tolist())
-        _native.adam_step(p, m, v, g, t)
-    np.testing.assert_allclose(np.array(res[0][0]), np.array(hist), rtol=1e-5)
-    np.testing.assert_allclose(np.array(res[0][1]), p.cpu().numpy(), rtol=1e-4, atol=1e-6)
+    _check_against_one_gpu(res[0], p, target)
