@@ -35,7 +35,7 @@ constexpr int kWarps = (kTile / kBlockW) * (kTile / kBlockH);
 constexpr int kThreads = kWarps * 32;
 constexpr int kChunk = 128;                              // triangles binned per round (<= kThreads)
 constexpr int kBlocksPerTile = kWarps;                    // 2 columns x 4 rows of warp blocks
-constexpr int kRegionBlocks = 4 * kBlocksPerTile;        // region kernel: 2 x 2 tiles
+constexpr int kRegionCols = 2;                           // region kernel: 2 tiles wide
 static_assert(kBlocksPerTile == 8, "tile block codes are stored as one 64-bit word");
 constexpr float kRenorm = 18446744073709551616.0f;        // 2^64
 constexpr float kRenormInv = 5.42101086242752217e-20f;    // 2^-64
@@ -196,8 +196,8 @@ __global__ void __launch_bounds__(kSetupThreads) dr_setup_kernel(
 // the list walks (forward_walk, gradient_walk):
 //   tile kernel    one CTA per (scene, 16x16 tile[, triangle block]), 8 warps,
 //                  warp w on block w; long lists binned in chunks
-//   region kernel  one CTA per (scene, 2x2 tiles) for lists within one chunk;
-//                  warps take the region's 32 blocks from a shared counter
+//   region kernel  one CTA per (scene, 2x1 tiles) for lists within one chunk;
+//                  warps take the region's 16 blocks from a shared counter
 // Triangles are binned in order (build_list, build_region_list) and every
 // kept entry carries a one-byte code per warp block, decided once at binning
 // time from the block's rectangle against the triangle's box and edge lines:
@@ -226,16 +226,17 @@ struct Smem {
   int is_last;
 };
 
-// Region kernel (a list of at most kChunk triangles): one CTA per 2 x 2
-// tiles, one code per warp block of the region, warps taking blocks from a
-// shared counter.
+// Region kernel (a list of at most kChunk triangles): one CTA per region of
+// 2 x kRows tiles (kRB = 16 kRows warp blocks), one code per warp block of the
+// region, warps taking blocks from a shared counter.
+template <int kRB>
 struct RegionSmem {
   TriRec rec[kChunk];
-  unsigned char bcode[kChunk][kRegionBlocks];
+  unsigned char bcode[kChunk][kRB];
   int kidx[kChunk];
   float acc[kChunk][kParams];
   int warp_count[kWarps];
-  double loss_part[kRegionBlocks];
+  double loss_part[kRB];
   int next_block;
   int is_last;
 };
@@ -318,9 +319,9 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
   return total;
 }
 
-// Pixel origin of warp block `blk` of a region: 4 tiles of 8 blocks in the
-// order left-top, right-top, left-bottom, right-bottom; each tile's blocks as
-// the tile kernel's warps (2 columns x 4 rows). A block on a tile row the
+// Pixel origin of warp block `blk` of a region: tiles of 8 blocks in the
+// order left-top, right-top[, left-bottom, right-bottom]; each tile's blocks
+// as the tile kernel's warps (2 columns x 4 rows). A block on a tile row the
 // launch does not cover gets y0 = H: empty.
 __device__ __forceinline__ void region_block_origin(const RasterArgs& a, int rx0, int lrow0,
                                                     int blk, int& x0, int& y0) {
@@ -332,15 +333,17 @@ __device__ __forceinline__ void region_block_origin(const RasterArgs& a, int rx0
 }
 
 // The region's whole list (a.T <= kChunk), in order: two threads per
-// triangle, each classifying 16 of the 32 blocks. Also clears the gradient
+// triangle, each classifying half of the kRB blocks. Also clears the gradient
 // accumulators.
-__device__ int build_region_list(RegionSmem& sm, const RasterArgs& a,
+template <int kRB>
+__device__ int build_region_list(RegionSmem<kRB>& sm, const RasterArgs& a,
                                  const TriRec* __restrict__ recs, int rx0, int lrow0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int half = threadIdx.x & 1;
   const int k = (int)threadIdx.x >> 1;
-  constexpr int kPer = kRegionBlocks / 2;
-  static_assert(kPer == 16 && kThreads / 2 == kChunk, "two threads per triangle, 16 blocks each");
+  constexpr int kPer = kRB / 2;
+  static_assert((kPer == 8 || kPer == 16) && kThreads / 2 == kChunk,
+                "two threads per triangle, 8 or 16 blocks each");
   bool keep_half = false;
   unsigned long long lo = 0x0101010101010101ull, hi = lo;  // all kBlkSkip
   const TriRec* r = recs + k;
@@ -375,7 +378,7 @@ __device__ int build_region_list(RegionSmem& sm, const RasterArgs& a,
     const int slot = base + __popc(ballot & ((1u << (lane & ~1)) - 1u));
     unsigned long long* dst_code = reinterpret_cast<unsigned long long*>(&sm.bcode[slot][half * kPer]);
     dst_code[0] = lo;
-    dst_code[1] = hi;
+    if (kPer == 16) dst_code[1] = hi;
     if (!half) {
       sm.kidx[slot] = k;
       const float4* src = reinterpret_cast<const float4*>(r);
@@ -1357,28 +1360,30 @@ __device__ __forceinline__ int center_out(int k, int n) {
 }
 
 // Region kernel, for scenes whose whole list fits one chunk (T <= kChunk):
-// one CTA per (scene, 2 x 2 tiles), the list binned once for all 32 warp
-// blocks, warps taking blocks from a shared counter. A warp that finishes a
-// cheap block takes the next one instead of waiting for the CTA's busiest
-// warp; there is no barrier between the list and the final flush.
-template <int Mode, int kPrec>
+// one CTA per (scene, 2 x kRows tiles), the list binned once for all of the
+// region's warp blocks, warps taking blocks from a shared counter. A warp that
+// finishes a cheap block takes the next one instead of waiting for the CTA's
+// busiest warp; there is no barrier between the list and the final flush.
+template <int Mode, int kPrec, int kRows>
 __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArgs a) {
+  constexpr int kRB = kRegionCols * kRows * kBlocksPerTile;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  RegionSmem& sm = *reinterpret_cast<RegionSmem*>(smem_raw);
+  RegionSmem<kRB>& sm = *reinterpret_cast<RegionSmem<kRB>*>(smem_raw);
   if (a.skip_flag && *a.skip_flag) return;
 
   // 1-D grid over (region, scene), scenes fastest and regions centre-out:
   // central regions carry the most overlapping geometry, and the light edge
   // regions then fill the tail of the launch.
-  const int regions_x = (a.tiles_x + 1) >> 1, regions_y = (a.tile_rows + 1) >> 1;
+  const int regions_x = (a.tiles_x + kRegionCols - 1) / kRegionCols;
+  const int regions_y = (a.tile_rows + kRows - 1) / kRows;
   const int n_regions = regions_x * regions_y;
   const int b = (int)(blockIdx.x % (unsigned)a.B);
   const int rank = (int)(blockIdx.x / (unsigned)a.B);
   const int rx = center_out(rank % regions_x, regions_x);
   const int ry = center_out(rank / regions_x, regions_y);
   const int region = ry * regions_x + rx;
-  const int rx0 = rx * 2 * kTile;
-  const int lrow0 = ry * 2;
+  const int rx0 = rx * kRegionCols * kTile;
+  const int lrow0 = ry * kRows;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   Consts K;
   K.sigma_eff = a.sigma_eff;
@@ -1387,10 +1392,10 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArg
   if (threadIdx.x == 0) sm.next_block = kWarps;
   const int count = build_region_list(sm, a, a.recs + (size_t)b * a.T, rx0, lrow0);
 
-  // Blocks are taken at most once each, so no warp runs more than
-  // kRegionBlocks iterations.
+  // Blocks are taken at most once each, so no warp runs more than kRB
+  // iterations.
   int blk = warp;
-  for (int it = 0; it < kRegionBlocks; ++it) {
+  for (int it = 0; it < kRB; ++it) {
     int x0, y0;
     region_block_origin(a, rx0, lrow0, blk, x0, y0);
     const int px = x0 + (lane & 7), py = y0 + (lane >> 3);
@@ -1420,14 +1425,14 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArg
     int next = 0;
     if (lane == 0) next = atomicAdd(&sm.next_block, 1);
     blk = __shfl_sync(0xffffffffu, next, 0);
-    if (blk >= kRegionBlocks) break;
+    if (blk >= kRB) break;
   }
 
   if (Mode == kModeRender) return;
   __syncthreads();
   flush_grads(sm, a, b, count);
   if (Mode == kModeLoss)
-    scene_loss(a, b, region, n_regions, sm.loss_part, kRegionBlocks, sm.loss_part, &sm.is_last);
+    scene_loss(a, b, region, n_regions, sm.loss_part, kRB, sm.loss_part, &sm.is_last);
 }
 
 // ---------------------------------------------------------------------------
@@ -1628,7 +1633,7 @@ cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
 
 static_assert(sizeof(Smem) <= 48 * 1024, "raster smem must fit the default 48 KB limit");
 
-static_assert(sizeof(RegionSmem) <= 48 * 1024, "region smem must fit the default 48 KB limit");
+static_assert(sizeof(RegionSmem<32>) <= 48 * 1024, "region smem must fit the default 48 KB limit");
 
 // SMs of the current device (cached per device).
 static int device_sms() {
@@ -1651,14 +1656,23 @@ static int device_sms() {
 
 // The region kernel when the whole list fits one chunk (T <= kChunk) and the
 // launch spans at least two full waves of its CTAs (4 per SM): a region CTA
-// works 4 tiles, so with fewer CTAs the slowest one sets the time and the
-// tile kernel's 4x finer grid is faster. Otherwise the tile kernel.
+// works several tiles, so with fewer CTAs the slowest one sets the time and
+// the tile kernel's finer grid is faster. Otherwise the tile kernel.
+// Regions of 2 x 1 tiles: a 2 x 2 region CTA averaged ~150 us at the headline
+// size (3.5 waves), and SMs that ran out of CTAs idled for up to 100 us while
+// the last ones finished. Halving the unit halves that tail; the list is
+// binned twice as often, for about 2 % more work.
+constexpr int kRegionRows = 1;
 template <int Mode, int kPrec>
 static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
-  const long long n_ctas = (long long)((a.tiles_x + 1) / 2) * ((a.tile_rows + 1) / 2) * a.B;
+  constexpr int kRows = kRegionRows;
+  constexpr int kRB = kRegionCols * kRows * kBlocksPerTile;
+  const long long n_ctas = (long long)((a.tiles_x + kRegionCols - 1) / kRegionCols) *
+                           ((a.tile_rows + kRows - 1) / kRows) * a.B;
   if (a.T <= kChunk && n_ctas >= 8LL * device_sms()) {
     if (n_ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    dr_raster_region_kernel<Mode, kPrec><<<(unsigned)n_ctas, kThreads, sizeof(RegionSmem), s>>>(a);
+    dr_raster_region_kernel<Mode, kPrec, kRows>
+        <<<(unsigned)n_ctas, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);
     return cudaGetLastError();
   }
   dim3 grid(n_tiles, a.B);
