@@ -1655,9 +1655,11 @@ static int device_sms() {
 }
 
 // The region kernel when the whole list fits one chunk (T <= kChunk) and the
-// launch spans at least two full waves of its CTAs (4 per SM): a region CTA
-// works several tiles, so with fewer CTAs the slowest one sets the time and
-// the tile kernel's finer grid is faster. Otherwise the tile kernel.
+// launch fills at least one wave of its CTAs (4 per SM): a region CTA works
+// two tiles, so with fewer CTAs the slowest one sets the time and the tile
+// kernel's finer grid is faster (measured at 256^2, T = 128: 4 scenes, 512
+// region CTAs, take 0.133 ms on the tile kernel and 0.152 ms on the region
+// kernel; 8 scenes, 1024 CTAs, 0.199 and 0.189 ms). Otherwise the tile kernel.
 // Regions of 2 x 1 tiles: a 2 x 2 region CTA averaged ~150 us at the headline
 // size (3.5 waves), and SMs that ran out of CTAs idled for up to 100 us while
 // the last ones finished. Halving the unit halves that tail; the list is
@@ -1669,7 +1671,7 @@ static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s)
   constexpr int kRB = kRegionCols * kRows * kBlocksPerTile;
   const long long n_ctas = (long long)((a.tiles_x + kRegionCols - 1) / kRegionCols) *
                            ((a.tile_rows + kRows - 1) / kRows) * a.B;
-  if (a.T <= kChunk && n_ctas >= 8LL * device_sms()) {
+  if (a.T <= kChunk && n_ctas >= 4LL * device_sms()) {
     if (n_ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     dr_raster_region_kernel<Mode, kPrec, kRows>
         <<<(unsigned)n_ctas, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);

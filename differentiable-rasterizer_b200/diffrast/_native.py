@@ -293,15 +293,25 @@ def _side_streams(dev: torch.device):
     return s
 
 
+def host_chunks(batch: int) -> list[tuple[int, int]]:
+    """Scene ranges [lo, hi) of the pipelined host path: cuts at 1/8, 3/8, 5/8
+    and 7/8 of the batch, so the first and last chunks are half the others
+    (32 scenes: 4, 8, 8, 8, 4). The first chunk's upload and the last chunk's
+    computation overlap nothing; halving them shortens the whole call."""
+    cuts = sorted({0, batch, *(int(batch * f + 0.5) for f in (0.125, 0.375, 0.625, 0.875))})
+    return [(lo, hi) for lo, hi in zip(cuts, cuts[1:]) if hi > lo]
+
+
 def _loss_backward_from_host(params: torch.Tensor, targets: torch.Tensor, sigma: float,
                              background, layout: int, dev: torch.device):
     """dr_loss_backward on host tensors, pipelined over scene chunks.
 
-    Scenes are independent, so the batch is cut into up to four chunks. Each
-    chunk's upload runs on a copy stream. Its kernel waits only for that upload
-    and runs on one of two compute streams, so chunk c computes while chunk
-    c + 1 uploads, and the tail of one chunk's kernel overlaps the next.
-    Results stay on the device; the caller's stream waits for all chunks.
+    Scenes are independent, so the batch is cut into up to five chunks
+    (host_chunks). Each chunk's upload runs on a copy stream. Its kernel waits
+    only for that upload and runs on one of two compute streams, so chunk c
+    computes while chunk c + 1 uploads, and the tail of one chunk's kernel
+    overlaps the next. Results stay on the device; the caller's stream waits
+    for all chunks.
     """
     p = params.detach().to(torch.float32).contiguous()
     t = targets.detach().to(torch.float32).contiguous()
@@ -321,10 +331,7 @@ def _loss_backward_from_host(params: torch.Tensor, targets: torch.Tensor, sigma:
     copy_s.wait_stream(cur)
     for s in comp:
         s.wait_stream(cur)
-    n_chunks = min(4, B)
-    step = -(-B // n_chunks)
-    for c, lo in enumerate(range(0, B, step)):
-        hi = min(B, lo + step)
+    for c, (lo, hi) in enumerate(host_chunks(B)):
         with torch.cuda.stream(copy_s):
             p_d[lo:hi].copy_(p[lo:hi], non_blocking=True)
             t_d[lo:hi].copy_(t[lo:hi], non_blocking=True)

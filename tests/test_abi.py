@@ -90,3 +90,15 @@ def test_argument_errors_need_no_device():
                                        None) == _native.INVALID_ARGUMENT
     assert L.dr_triangle_block_backward(None, None, None, 0, 1, 1, 8, 8, 0.01, 2, 1, None, None, 0,
                                         0, None, None, None, None) == _native.INVALID_ARGUMENT
+
+
+def test_host_chunks_cover_the_batch_in_order():
+    from diffrast._native import host_chunks
+
+    for b in range(2, 130):
+        ch = host_chunks(b)
+        assert ch[0][0] == 0 and ch[-1][1] == b
+        assert all(lo < hi for lo, hi in ch)
+        assert all(ch[i][1] == ch[i + 1][0] for i in range(len(ch) - 1))
+        assert len(ch) <= 5
+    assert [hi - lo for lo, hi in host_chunks(32)] == [4, 8, 8, 8, 4]
