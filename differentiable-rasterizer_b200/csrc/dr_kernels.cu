@@ -420,7 +420,7 @@ struct PairEval {
   int edge;
 };
 
-// Reciprocal and square root rounded to nearest without the library's
+// Quotients and square roots rounded to nearest without the library's
 // special-case branches: the hardware approximation (rcp.approx / rsqrt.approx,
 // relative error below 2^-22) refined by one Newton-Raphson step with an FMA
 // residual (Markstein's method). The refined value is within ~2^-44 of the
@@ -436,10 +436,6 @@ __device__ __forceinline__ float rsqrt_approx(float x) {
   asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
-__device__ __forceinline__ float rcp_nr(float y) {
-  const float r = rcp_approx(y);
-  return __fmaf_rn(r, __fmaf_rn(-y, r, 1.0f), r);
-}
 // sqrt(x) for x >= 0; inputs below 1e-30 (distances far under the 1e-9 cut
 // of grad.rs:252) return 0.
 __device__ __forceinline__ float sqrt_nr(float x) {
@@ -450,9 +446,9 @@ __device__ __forceinline__ float sqrt_nr(float x) {
   return x > 1e-30f ? out : 0.0f;
 }
 
-// a / b rounded to nearest, given inv_b = RN(1 / b): one correction step on
-// the product (an FMA residual), which yields the correctly rounded quotient
-// except in rare boundary cases.
+// a / b rounded to nearest, given inv_b within 2^-22 of 1 / b (rcp_approx, or
+// a precomputed RN(1 / b)): one correction step on the product with an FMA
+// residual. For a = 1 this is the Newton-refined reciprocal.
 __device__ __forceinline__ float div_rn_inv(float a, float b, float inv_b) {
   const float q0 = __fmul_rn(a, inv_b);
   const float r = __fmaf_rn(-q0, b, a);
@@ -467,8 +463,7 @@ __device__ __forceinline__ float div_rn_inv(float a, float b, float inv_b) {
 __device__ __forceinline__ float sigmoid_rounded(float x) {
   const float e = __expf(-fabsf(x));
   const float y = __fadd_rn(1.0f, e);
-  const float ry = rcp_nr(y);
-  return x >= 0.0f ? ry : div_rn_inv(e, y, ry);
+  return div_rn_inv(x >= 0.0f ? 1.0f : e, y, rcp_approx(y));
 }
 
 __device__ __forceinline__ float sigmoid_fast(float x) {
@@ -485,7 +480,7 @@ __device__ __forceinline__ void cov_grad_ref(const TriRec& r, int edge, float t,
   const float ax = r.v[2 * edge], ay = r.v[2 * edge + 1];
   const float cpx = __fadd_rn(ax, __fmul_rn(t, r.e[2 * edge]));
   const float cpy = __fadd_rn(ay, __fmul_rn(t, r.e[2 * edge + 1]));
-  const float rd = rcp_nr(dist);
+  const float rd = rcp_approx(dist);
   const float ux = div_rn_inv(__fsub_rn(ptx, cpx), dist, rd);
   const float uy = div_rn_inv(__fsub_rn(pty, cpy), dist, rd);
   float chain = div_rn_inv(__fmul_rn(cov, __fsub_rn(1.0f, cov)), K.sigma_eff, K.inv_sigma);
