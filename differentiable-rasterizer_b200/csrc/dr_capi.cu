@@ -448,8 +448,7 @@ dr_status dr_triangle_block_forward(dr_ctx* ctx, const float* params, const floa
   st = prepare(ctx, params, background, bg_per_scene, B, T, H, W, sigma, DR_LAYOUT_BHWC, 1, a, s);
   if (st) return st;
   const int n_tiles = a.tiles_x * ((H + kTileSide - 1) / kTileSide);
-  DR_CUDA(launch_triangle_block(0, kModeLoss, a, n_tiles, n_blocks, block, (float4*)state, nullptr,
-                                s),
+  DR_CUDA(launch_triangle_block(0, kModeLoss, a, n_tiles, n_blocks, block, (float4*)state, s),
           "triangle-block forward");
   return DR_OK;
 }
@@ -486,10 +485,8 @@ dr_status dr_triangle_block_backward(dr_ctx* ctx, const float* params, const flo
     st = loss_scratch(ctx, a, n_tiles);
     if (st) return st;
   }
-  st = ensure(ctx, ctx->split, raster_split_bytes(B, 1, H, W), false);
-  if (st) return st;
   DR_CUDA(launch_triangle_block(1, mode, a, n_tiles, n_blocks, block,
-                                (float4*)const_cast<float*>(state), (float4*)ctx->split.ptr, s),
+                                (float4*)const_cast<float*>(state), s),
           "triangle-block backward");
   return DR_OK;
 }
@@ -700,10 +697,12 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
     chk(cudaMemsetAsync(M, 0, np * 4, cs));
     chk(cudaMemsetAsync(V, 0, np * 4, cs));
     chk(launch_fit_init(S, cs));
+    // Iteration 0's gradients and records; each iteration's Adam kernel then
+    // clears the gradients and writes the next iteration's records.
+    chk(cudaMemsetAsync(Gr, 0, np * 4, cs));
+    chk(launch_setup(P, T, W, H, sigma_at(cfg, 0), 1, (TriRec*)ctx->recs.ptr, cs));
     for (int i = 0; i < iters; ++i) {
       float sigma = sigma_at(cfg, i);
-      chk(cudaMemsetAsync(Gr, 0, np * 4, cs));
-      chk(launch_setup(P, T, W, H, sigma, 1, (TriRec*)ctx->recs.ptr, cs));
       RasterArgs a;
       memset(&a, 0, sizeof(a));
       a.recs = (const TriRec*)ctx->recs.ptr;
@@ -729,11 +728,15 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       a.losses = &S->loss;
       a.n_values = (double)H * (double)W * 3.0;
       a.skip_flag = &S->stopped;
+      a.fit = S;
+      a.fit_losses = L;
+      a.fit_patience = cfg->patience;
+      a.fit_min_delta = cfg->min_delta;
+      a.fit_iter = i;
       if (split_k > 1)
         chk(launch_raster_split(kModeLoss, a, tiles, split_k, (float4*)ctx->split.ptr, cs));
       else
         chk(launch_raster(kModeLoss, a, tiles, cs));
-      chk(launch_fit_control(S, i, cfg->min_delta, cfg->patience, L, cs));
       AdamArgs ad;
       memset(&ad, 0, sizeof(ad));
       ad.params = P;
@@ -768,7 +771,9 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       ad.run_flag = &S->run_adam;
       ad.copy_flag = &S->copy_best;
       ad.copy_dst = best_params;
-      chk(launch_adam(ad, cs));
+      const bool last = i + 1 == iters;
+      chk(launch_fit_adam_setup(ad, Gr, T, W, H, last ? sigma : sigma_at(cfg, i + 1),
+                                last ? nullptr : (TriRec*)ctx->recs.ptr, cs));
     }
     chk(cudaMemcpyAsync(final_params, P, np * 4, cudaMemcpyDeviceToDevice, cs));
     cudaGraph_t graph = nullptr;

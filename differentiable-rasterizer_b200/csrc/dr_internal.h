@@ -12,9 +12,13 @@ struct TriRec;
 
 enum RasterMode { kModeRender = 0, kModeLoss = 1, kModeGrad = 2,
                   // Triangle-block split (launch_raster_split): per (tile, block) forward
-                  // over black, then the per-block gradient pass.
-                  kModeSplitFwd = 3, kModeSplitBwd = 4 };
+                  // over black, then per (tile, block) the combine of every block's
+                  // forward state and the block's gradient pass, for the loss or for an
+                  // upstream image gradient.
+                  kModeSplitFwd = 3, kModeSplitBwd = 4, kModeSplitBwdGrad = 5 };
 enum Layout { kLayoutBHWC = 0, kLayoutBCHW = 1 };
+
+struct FitState;
 
 struct RasterArgs {
   const TriRec* recs;  // B*T records from the set-up kernel
@@ -41,9 +45,14 @@ struct RasterArgs {
   const int* skip_flag;       // optional: nonzero -> the kernel does nothing
   int split_k;                // triangle blocks of a split launch (else 0)
   int split_base;             // first block of this launch (grid z adds to it)
-  int split_own;              // >= 0: only this block's backward state is kept
-  float4* split_fwd;          // per (block, scene, pixel): 2 float4 of forward state
-  float4* split_bwd;          // per (block or 1, scene, pixel): 2 float4 from the combine
+  float4* split_state;        // per (block, scene, pixel): 2 float4 of forward state
+  // dr_fit only (B = 1): the CTA that completes the loss also runs Fitter::step's
+  // bookkeeping for iteration fit_iter (fit.rs:243-288).
+  FitState* fit;
+  float* fit_losses;
+  long long fit_patience;     // < 0: none
+  float fit_min_delta;
+  int fit_iter;
 };
 
 struct AdamArgs {
@@ -79,8 +88,11 @@ size_t raster_smem_bytes();
 // Sets the calling thread's dr_last_error() message.
 void set_last_error(const char* msg);
 cudaError_t launch_fit_init(FitState* st, cudaStream_t s);
-cudaError_t launch_fit_control(FitState* st, int iter, float min_delta, long long patience,
-                               float* losses, cudaStream_t s);
+// One fit iteration's Adam step (skipped unless the fit state says run) and
+// the next iteration's set-up at next_sigma, one thread per triangle; also
+// clears the gradients for the next raster launch. recs null: no set-up.
+cudaError_t launch_fit_adam_setup(const AdamArgs& a, float* grads, int T, int W, int H,
+                                  float next_sigma, TriRec* recs, cudaStream_t s);
 size_t tri_rec_bytes();
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
                          int tape_semantics, TriRec* recs, cudaStream_t s);
@@ -88,26 +100,24 @@ cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream
 // Triangle blocks for a loss/grad launch over all tile rows of B scenes: 1 when
 // the plain launch fills the GPU, else up to 8 (at least 32 triangles each).
 int raster_split_blocks(int B, int T, int n_tiles);
-// Bytes of split state a launch with k blocks needs (4 float4 per scene, block
+// Bytes of split state a launch with k blocks needs (2 float4 per scene, block
 // and pixel).
 inline size_t raster_split_bytes(int B, int k, int H, int W) {
-  return (size_t)B * k * H * W * 4 * sizeof(float4);
+  return (size_t)B * k * H * W * 2 * sizeof(float4);
 }
-// kModeLoss / kModeGrad as three launches over k triangle blocks: forward per
-// (tile, block) over black, a per-pixel combine of the blocks' affine maps
-// (final colour, loss, canvas entering each block, attenuation from the blocks
-// above), then the gradient pass per (tile, block). All tile rows (row0 0,
-// step 1).
+// kModeLoss / kModeGrad as two launches over k triangle blocks: forward per
+// (tile, block) over black into the split state; then per (tile, block) the
+// per-pixel combine of the blocks' affine maps (final colour, loss, canvas
+// entering the block, attenuation from the blocks above) and the block's
+// gradient pass. All tile rows (row0 0, step 1).
 cudaError_t launch_raster_split(int mode, const RasterArgs& a, int n_tiles, int k, float4* split,
                                 cudaStream_t s);
 // One GPU's share of a scene batch sharded by triangle blocks: phase 0 runs
-// block `block`'s forward over all pixels into its slice of fwd_state
+// block `block`'s forward over all pixels into its slice of `state`
 // (n_blocks x B x H x W x 32 bytes); phase 1, with every slice present, runs
-// the combine (final colour, loss) and the block's gradient pass, using
-// bwd_state (B x H x W x 32 bytes) as scratch.
+// the combine (final colour, loss) and the block's gradient pass.
 cudaError_t launch_triangle_block(int phase, int mode, const RasterArgs& a, int n_tiles,
-                                  int n_blocks, int block, float4* fwd_state, float4* bwd_state,
-                                  cudaStream_t s);
+                                  int n_blocks, int block, float4* state, cudaStream_t s);
 // Per-image MSE scratch: B * mse_partials_per_image(n) doubles and B counters
 // (zero between launches; the kernel leaves them zero).
 size_t mse_partials_per_image(long long n);

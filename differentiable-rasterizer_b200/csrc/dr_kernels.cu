@@ -1125,6 +1125,44 @@ __device__ __forceinline__ void flush_grads(const S& sm, const RasterArgs& a, in
   }
 }
 
+// Fitter::step's bookkeeping after iteration `iter`'s loss (fit.rs:243-288):
+// record the loss, track the best, stop on divergence or patience, and tell
+// the next Adam step whether to run and to copy the best parameters first.
+__device__ void fit_control(FitState* st, int iter, float min_delta, long long patience,
+                            float* losses) {
+  if (st->stopped) {
+    st->run_adam = 0;
+    st->copy_best = 0;
+    return;
+  }
+  const float loss = st->loss;
+  if (!isfinite(loss)) {  // fit.rs:262-265
+    st->stopped = 1;
+    st->stop_reason = 2;
+    st->run_adam = 0;
+    st->copy_best = 0;
+    return;
+  }
+  losses[st->count] = loss;
+  st->count += 1;
+  if (__fadd_rn(loss, min_delta) < st->best_loss) {  // fit.rs:268-275
+    st->best_loss = loss;
+    st->best_iter = iter;
+    st->since = 0;
+    st->copy_best = 1;
+  } else {
+    st->since += 1;
+    st->copy_best = 0;
+  }
+  if (patience >= 0 && (long long)st->since >= patience) {  // fit.rs:278-281
+    st->stopped = 1;
+    st->stop_reason = 1;
+    st->run_adam = 0;
+    return;
+  }
+  st->run_adam = 1;
+}
+
 // Per-scene loss: each CTA's f64 partial (slot `slot` of the scene's n_blocks),
 // summed in fixed order by the scene's last CTA (canvas.rs:45-59). `part`
 // holds this CTA's n_part partials in shared memory; all threads call it after
@@ -1157,26 +1195,18 @@ __device__ __forceinline__ void scene_loss(const RasterArgs& a, int b, int slot,
       if (a.loss_sums) a.loss_sums[b] = tot;
       if (a.losses) a.losses[b] = (float)(tot / a.n_values);  // canvas.rs:58
       a.loss_counters[b] = 0;
+      if (a.fit) fit_control(a.fit, a.fit_iter, a.fit_min_delta, a.fit_patience, a.fit_losses);
     }
   }
 }
 
 // Split state, block-major so that one block's slice is contiguous (ranks of
-// a triangle-sharded scene all-gather their slices):
-//   forward  [c0 c1 c2 m] [e z0 zn -] per (block, scene, pixel): the block's
-//            composite over black and running product (its forward pass);
-//   backward [g0 g1 g2 -] [d0 d1 d2 a] per (block, scene, pixel): from the
-//            combine, the gradient reaching the block, the canvas entering it
-//            and the block's map factor a. With split_own >= 0 only that
-//            block's backward state is kept (slice 0).
-__device__ __forceinline__ float4* split_fwd_pixel(const RasterArgs& a, int k, int b, int px,
-                                                   int py) {
-  return a.split_fwd + (((size_t)k * a.B + b) * a.H * a.W + (size_t)py * a.W + px) * 2;
-}
-__device__ __forceinline__ float4* split_bwd_pixel(const RasterArgs& a, int k, int b, int px,
-                                                   int py) {
-  const int slot = a.split_own >= 0 ? 0 : k;
-  return a.split_bwd + (((size_t)slot * a.B + b) * a.H * a.W + (size_t)py * a.W + px) * 2;
+// a triangle-sharded scene all-gather their slices): [c0 c1 c2 m] [e z0 zn -]
+// per (block, scene, pixel), the block's composite over black and its running
+// product from its forward pass.
+__device__ __forceinline__ float4* split_pixel(const RasterArgs& a, int k, int b, int px,
+                                               int py) {
+  return a.split_state + (((size_t)k * a.B + b) * a.H * a.W + (size_t)py * a.W + px) * 2;
 }
 
 // Factor a of a block's map x -> a x + c from its forward state: NaN after a
@@ -1193,7 +1223,9 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   if (a.skip_flag && *a.skip_flag) return;
-  constexpr bool kSplit = Mode == kModeSplitFwd || Mode == kModeSplitBwd;
+  constexpr bool kSplitBwd = Mode == kModeSplitBwd || Mode == kModeSplitBwdGrad;
+  constexpr bool kSplit = Mode == kModeSplitFwd || kSplitBwd;
+  constexpr bool kLoss = Mode == kModeLoss || Mode == kModeSplitBwd;
 
   const int b = blockIdx.y;
   const int local_tile = blockIdx.x;
@@ -1211,6 +1243,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   K.inv_sigma = a.inv_sigma;
   // Triangles [t0, t1): all of them, or block kb of a split launch.
   const int kb = a.split_base + (int)blockIdx.z;
+  const bool lead = !kSplitBwd || blockIdx.z == 0;  // writes the image and the loss
   int t0 = 0, t1 = a.T;
   if (kSplit) {
     const int per = (a.T + a.split_k - 1) / a.split_k;
@@ -1224,7 +1257,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   float G0 = 0.0f, G1 = 0.0f, G2 = 0.0f;
   float r0, r1, r2;
 
-  if (Mode != kModeSplitBwd) {
+  if (!kSplitBwd) {
     // ---- pass 1: forward composite ----------------------------------------
     float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;  // a block composites over black
     if (!kSplit) scene_background(a, b, c0, c1, c2);
@@ -1234,7 +1267,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     }
     if (Mode == kModeSplitFwd) {
       if (active) {
-        float4* sp = split_fwd_pixel(a, kb, b, px, py);
+        float4* sp = split_pixel(a, kb, b, px, py);
         sp[0] = make_float4(c0, c1, c2, P.m);
         sp[1] = make_float4(__int_as_float(P.e), __int_as_float(P.z0), __int_as_float(P.zn), 0.f);
       }
@@ -1252,23 +1285,52 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     }
     scene_background(a, b, r0, r1, r2);
   } else {
-    // The block's running product from its forward, and from the combine the
-    // gradient reaching the block and the canvas entering it.
+    // The combine, per pixel from every block's forward state. Block k's
+    // layers map the canvas beneath them to a_k x + c_k, a_k the product of
+    // their (1 - w) (0 after an opaque layer, NaN after a NaN one, as the
+    // reference's running composite propagates them) and c_k their composite
+    // over black. The canvas entering block kb is the composition of the maps
+    // below it applied to the background, the final colour the composition of
+    // all; the gradient reaching block kb is G times the product of a_k over
+    // the blocks above, taken from the top down. The CTAs of the launch's
+    // first block write the image and the loss.
     r0 = r1 = r2 = 0.0f;
+    double sq = 0.0;
     if (active) {
-      const float4* sf = split_fwd_pixel(a, kb, b, px, py);
-      const float4* sb = split_bwd_pixel(a, kb, b, px, py);
-      const float4 s0 = sf[0], s1 = sf[1], s2 = sb[0], s3 = sb[1];
-      P.m = s0.w;
-      P.e = __float_as_int(s1.x);
-      P.z0 = __float_as_int(s1.y);
-      P.zn = __float_as_int(s1.z);
-      G0 = s2.x;
-      G1 = s2.y;
-      G2 = s2.z;
-      r0 = s3.x;
-      r1 = s3.y;
-      r2 = s3.z;
+      float d0, d1, d2;
+      scene_background(a, b, d0, d1, d2);
+      for (int k = 0; k < a.split_k; ++k) {
+        const float4* sf = split_pixel(a, k, b, px, py);
+        const float4 s0 = sf[0], s1 = sf[1];
+        if (k == kb) {
+          r0 = d0;
+          r1 = d1;
+          r2 = d2;
+          P.m = s0.w;
+          P.e = __float_as_int(s1.x);
+          P.z0 = __float_as_int(s1.y);
+          P.zn = __float_as_int(s1.z);
+        }
+        const float f = block_factor(s0, s1);
+        d0 = __fadd_rn(__fmul_rn(f, d0), s0.x);
+        d1 = __fadd_rn(__fmul_rn(f, d1), s0.y);
+        d2 = __fadd_rn(__fmul_rn(f, d2), s0.z);
+      }
+      if (lead && a.image) store_pixel(a, b, px, py, d0, d1, d2);
+      top_gradient<kLoss ? kModeLoss : kModeGrad>(a, b, px, py, true, d0, d1, d2, G0, G1, G2,
+                                                   sq);
+      float above = 1.0f;
+      for (int k = a.split_k - 1; k > kb; --k) {
+        const float4* sf = split_pixel(a, k, b, px, py);
+        above = __fmul_rn(above, block_factor(sf[0], sf[1]));
+      }
+      G0 = __fmul_rn(G0, above);
+      G1 = __fmul_rn(G1, above);
+      G2 = __fmul_rn(G2, above);
+    }
+    if (kLoss && lead) {
+      const double ws = warp_sum_d(sq);
+      if (lane == 0) sm.loss_part[warp] = ws;
     }
   }
 
@@ -1276,7 +1338,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   Prod Q;
   Q.init();
   for (int ci = 0; ci < n_chunks; ++ci) {
-    if (n_chunks > 1 || Mode == kModeSplitBwd) {
+    if (n_chunks > 1 || kSplitBwd) {
       __syncthreads();
       count = build_list(sm, recs, t1, t0 + ci * kChunk, tx0, ty0, a.W, a.H);
     }
@@ -1288,63 +1350,8 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     flush_grads(sm, a, b, count);
   }
 
-  if (Mode == kModeLoss)
+  if (kLoss && lead)
     scene_loss(a, b, blockIdx.x, gridDim.x, sm.loss_part, kWarps, sm.loss_part, &sm.is_last);
-}
-
-// Combine of a split launch, one thread per pixel (CTA = tile). Block k's
-// layers map the canvas beneath them to a_k x + c_k, a_k the product of their
-// (1 - w) (0 after an opaque layer, NaN after a NaN one, as the reference's
-// running composite propagates them) and c_k their composite over black. The
-// canvas entering block k is the composition of the maps below applied to the
-// background; the final colour is the composition of all. The gradient
-// reaching block k is G times the product of a_j over the blocks above.
-template <int Mode>
-__global__ void __launch_bounds__(kThreads) dr_split_combine_kernel(RasterArgs a) {
-  __shared__ double loss_part[kWarps];
-  __shared__ int is_last;
-  if (a.skip_flag && *a.skip_flag) return;
-  const int b = blockIdx.y;
-  const int tile_col = blockIdx.x % a.tiles_x;
-  const int tile_row = a.tile_row0 + (blockIdx.x / a.tiles_x) * a.tile_row_step;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int px = tile_col * kTile + (warp & 1) * kBlockW + (lane & 7);
-  const int py = tile_row * kTile + (warp >> 1) * kBlockH + (lane >> 3);
-  const bool active = px < a.W && py < a.H;
-  double sq = 0.0;
-  if (active) {
-    float d0, d1, d2;
-    scene_background(a, b, d0, d1, d2);
-    // Block factors are recomputed from the forward state on the way back
-    // (L2-resident loads) rather than held in a dynamically indexed array.
-    const int kk = a.split_k;
-    for (int k = 0; k < kk; ++k) {
-      const float4* sf = split_fwd_pixel(a, k, b, px, py);
-      const float4 s0 = __ldcg(sf), s1 = __ldcg(sf + 1);
-      const float f = block_factor(s0, s1);
-      if (a.split_own < 0 || k == a.split_own)
-        split_bwd_pixel(a, k, b, px, py)[1] = make_float4(d0, d1, d2, f);
-      d0 = __fadd_rn(__fmul_rn(f, d0), s0.x);
-      d1 = __fadd_rn(__fmul_rn(f, d1), s0.y);
-      d2 = __fadd_rn(__fmul_rn(f, d2), s0.z);
-    }
-    if (a.image) store_pixel(a, b, px, py, d0, d1, d2);
-    float G0, G1, G2;
-    top_gradient<Mode>(a, b, px, py, true, d0, d1, d2, G0, G1, G2, sq);
-    float above = 1.0f;
-    for (int k = kk - 1; k >= 0; --k) {
-      if (a.split_own < 0 || k == a.split_own)
-        split_bwd_pixel(a, k, b, px, py)[0] =
-            make_float4(__fmul_rn(G0, above), __fmul_rn(G1, above), __fmul_rn(G2, above), 0.f);
-      const float4* sf = split_fwd_pixel(a, k, b, px, py);
-      above = __fmul_rn(above, block_factor(__ldcg(sf), __ldcg(sf + 1)));
-    }
-  }
-  if (Mode == kModeLoss) {
-    const double ws = warp_sum_d(sq);
-    if (lane == 0) loss_part[warp] = ws;
-    scene_loss(a, b, blockIdx.x, gridDim.x, loss_part, kWarps, loss_part, &is_last);
-  }
 }
 
 // k-th index of 0..n-1 in centre-out order: c, c-1, c+1, c-2, c+2, ...
@@ -1549,6 +1556,30 @@ __global__ void dr_adam4_kernel(AdamArgs a) {
   reinterpret_cast<float4*>(a.params)[q] = P;
 }
 
+// dr_fit's Adam step (the per-element update of dr_adam_kernel) fused with
+// the next iteration's set-up: one thread per triangle updates its 10
+// parameters, clears their gradients for the next raster launch and writes
+// the triangle's record from the updated parameters.
+__global__ void __launch_bounds__(kSetupThreads) dr_fit_adam_setup_kernel(
+    AdamArgs a, float* __restrict__ grads, int T, int W, int H, float next_sigma,
+    TriRec* __restrict__ recs) {
+  const int t = blockIdx.x * kSetupThreads + (int)threadIdx.x;
+  if (t >= T) return;
+  const long long base = (long long)t * kParams;
+  if (a.copy_flag && *a.copy_flag)
+    for (int j = 0; j < kParams; ++j) a.copy_dst[base + j] = a.params[base + j];
+  if (a.run_flag && !*a.run_flag) return;
+  for (int j = 0; j < kParams; ++j) {
+    const long long i = base + j;
+    float m = a.m[i], v = a.v[i];
+    a.params[i] = adam_one(a, i, a.params[i], grads[i], m, v);
+    a.m[i] = m;
+    a.v[i] = v;
+    grads[i] = 0.0f;
+  }
+  if (recs) recs[t] = make_record(a.params, t, W, H, next_sigma, 1);
+}
+
 // ---------------------------------------------------------------------------
 // Fit bookkeeping (Fitter::step, fit.rs:243-288), one thread, no host sync
 // ---------------------------------------------------------------------------
@@ -1565,41 +1596,6 @@ __global__ void dr_fit_init_kernel(FitState* st) {
   st->copy_best = 0;
 }
 
-__global__ void dr_fit_control_kernel(FitState* st, int iter, float min_delta, long long patience,
-                                      float* losses) {
-  if (st->stopped) {
-    st->run_adam = 0;
-    st->copy_best = 0;
-    return;
-  }
-  const float loss = st->loss;
-  if (!isfinite(loss)) {  // fit.rs:262-265
-    st->stopped = 1;
-    st->stop_reason = 2;
-    st->run_adam = 0;
-    st->copy_best = 0;
-    return;
-  }
-  losses[st->count] = loss;
-  st->count += 1;
-  if (__fadd_rn(loss, min_delta) < st->best_loss) {  // fit.rs:268-275
-    st->best_loss = loss;
-    st->best_iter = iter;
-    st->since = 0;
-    st->copy_best = 1;
-  } else {
-    st->since += 1;
-    st->copy_best = 0;
-  }
-  if (patience >= 0 && (long long)st->since >= patience) {  // fit.rs:278-281
-    st->stopped = 1;
-    st->stop_reason = 1;
-    st->run_adam = 0;
-    return;
-  }
-  st->run_adam = 1;
-}
-
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
@@ -1611,12 +1607,15 @@ cudaError_t launch_fit_init(FitState* st, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-cudaError_t launch_fit_control(FitState* st, int iter, float min_delta, long long patience,
-                               float* losses, cudaStream_t s) {
-  dr_fit_control_kernel<<<1, 1, 0, s>>>(st, iter, min_delta, patience, losses);
+
+
+cudaError_t launch_fit_adam_setup(const AdamArgs& a, float* grads, int T, int W, int H,
+                                  float next_sigma, TriRec* recs, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  const int blocks = (T + kSetupThreads - 1) / kSetupThreads;
+  dr_fit_adam_setup_kernel<<<blocks, kSetupThreads, 0, s>>>(a, grads, T, W, H, next_sigma, recs);
   return cudaGetLastError();
 }
-
 
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
                          int tape_semantics, TriRec* recs, cudaStream_t s) {
@@ -1699,20 +1698,26 @@ int raster_split_blocks(int B, int T, int n_tiles) {
   return k < 2 ? 1 : (int)k;
 }
 
+// Split backward: per (tile, block) the combine and the block's gradient pass,
+// for the loss or for an upstream image gradient.
+template <int kPrec>
+static cudaError_t launch_split_bwd(int mode, const RasterArgs& a, dim3 grid, cudaStream_t s) {
+  if (mode == kModeLoss)
+    dr_raster_kernel<kModeSplitBwd, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  else
+    dr_raster_kernel<kModeSplitBwdGrad, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  return cudaGetLastError();
+}
+
 template <int kPrec>
 static cudaError_t launch_split_prec(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s) {
   RasterArgs f = a;
-  f.image = nullptr;  // the combine writes the image
-  dim3 grid3(n_tiles, a.B, a.split_k), grid2(n_tiles, a.B);
-  dr_raster_kernel<kModeSplitFwd, kPrec><<<grid3, kThreads, sizeof(Smem), s>>>(f);
-  cudaError_t e = cudaGetLastError();
+  f.image = nullptr;  // the backward's first block writes the image
+  const dim3 grid(n_tiles, a.B, a.split_k);
+  dr_raster_kernel<kModeSplitFwd, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(f);
+  const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (mode == kModeLoss) dr_split_combine_kernel<kModeLoss><<<grid2, kThreads, 0, s>>>(a);
-  else dr_split_combine_kernel<kModeGrad><<<grid2, kThreads, 0, s>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  dr_raster_kernel<kModeSplitBwd, kPrec><<<grid3, kThreads, sizeof(Smem), s>>>(f);
-  return cudaGetLastError();
+  return launch_split_bwd<kPrec>(mode, a, grid, s);
 }
 
 cudaError_t launch_raster_split(int mode, const RasterArgs& args, int n_tiles, int k, float4* split,
@@ -1725,9 +1730,7 @@ cudaError_t launch_raster_split(int mode, const RasterArgs& args, int n_tiles, i
   a.tile_rows = n_tiles / a.tiles_x;
   a.split_k = k;
   a.split_base = 0;
-  a.split_own = -1;
-  a.split_fwd = split;
-  a.split_bwd = split + (size_t)k * a.B * a.H * a.W * 2;
+  a.split_state = split;
   switch (a.precision) {
     case kPrecRef: return launch_split_prec<kPrecRef>(mode, a, n_tiles, s);
     case kPrecStrict: return launch_split_prec<kPrecStrict>(mode, a, n_tiles, s);
@@ -1739,36 +1742,28 @@ cudaError_t launch_raster_split(int mode, const RasterArgs& args, int n_tiles, i
 template <int kPrec>
 static cudaError_t launch_block_prec(int phase, int mode, const RasterArgs& a, int n_tiles,
                                      cudaStream_t s) {
-  dim3 grid3(n_tiles, a.B, 1), grid2(n_tiles, a.B);
+  const dim3 grid(n_tiles, a.B, 1);
   if (phase == 0) {
-    dr_raster_kernel<kModeSplitFwd, kPrec><<<grid3, kThreads, sizeof(Smem), s>>>(a);
+    RasterArgs f = a;
+    f.image = nullptr;
+    dr_raster_kernel<kModeSplitFwd, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(f);
     return cudaGetLastError();
   }
-  if (mode == kModeLoss) dr_split_combine_kernel<kModeLoss><<<grid2, kThreads, 0, s>>>(a);
-  else dr_split_combine_kernel<kModeGrad><<<grid2, kThreads, 0, s>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  RasterArgs f = a;
-  f.image = nullptr;
-  dr_raster_kernel<kModeSplitBwd, kPrec><<<grid3, kThreads, sizeof(Smem), s>>>(f);
-  return cudaGetLastError();
+  return launch_split_bwd<kPrec>(mode, a, grid, s);
 }
 
 cudaError_t launch_triangle_block(int phase, int mode, const RasterArgs& args, int n_tiles,
-                                  int n_blocks, int block, float4* fwd_state, float4* bwd_state,
-                                  cudaStream_t s) {
+                                  int n_blocks, int block, float4* state, cudaStream_t s) {
   if (args.B == 0 || n_tiles == 0) return cudaSuccess;
-  if (args.tiles_x <= 0 || n_blocks < 1 || block < 0 || block >= n_blocks || !fwd_state ||
-      (phase == 1 && (!bwd_state || (mode != kModeLoss && mode != kModeGrad))) ||
-      args.tile_row0 != 0 || args.tile_row_step != 1)
+  if (args.tiles_x <= 0 || n_blocks < 1 || block < 0 || block >= n_blocks || !state ||
+      (phase == 1 && mode != kModeLoss && mode != kModeGrad) || args.tile_row0 != 0 ||
+      args.tile_row_step != 1)
     return cudaErrorInvalidValue;
   RasterArgs a = args;
   a.tile_rows = n_tiles / a.tiles_x;
   a.split_k = n_blocks;
   a.split_base = block;
-  a.split_own = block;
-  a.split_fwd = fwd_state;
-  a.split_bwd = bwd_state;
+  a.split_state = state;
   switch (a.precision) {
     case kPrecRef: return launch_block_prec<kPrecRef>(phase, mode, a, n_tiles, s);
     case kPrecStrict: return launch_block_prec<kPrecStrict>(phase, mode, a, n_tiles, s);
