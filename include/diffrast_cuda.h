@@ -172,11 +172,12 @@ DR_API dr_status dr_loss_backward_sharded(dr_ctx* ctx, const float* params, cons
  * buffer of n_blocks * B * H * W * DR_TRIANGLE_BLOCK_STATE_BYTES bytes, block-major
  * (each slice contiguous, so ranks can all-gather their slices).
  *
- * dr_triangle_block_backward needs every slice of `state`. It combines the
- * blocks' per-pixel maps into the final image (optional `image`, layout as
- * `other`) and the per-scene loss (`losses`, when grad_input == 0). It then runs
- * block `block`'s gradient pass: `grads` (B, T, 10) is overwritten, nonzero only
- * on the block's triangles. `other` is the target (grad_input == 0, MSE as
+ * dr_triangle_block_backward needs every slice of `state` and only reads it.
+ * It combines the blocks' per-pixel maps into the final image (optional
+ * `image`, layout as `other`) and the per-scene loss (`losses`, when
+ * grad_input == 0). It then runs block `block`'s gradient pass: `grads`
+ * (B, T, 10) is overwritten, nonzero only on the block's triangles. `other`
+ * is the target (grad_input == 0, MSE as
  * dr_loss_backward) or the upstream image gradient (grad_input == 1, as
  * dr_grad_backward). The sum of `grads` over all blocks equals dr_loss_backward
  * to rounding. */
