@@ -318,7 +318,7 @@ def main():
     # e2e: public API with pinned host buffers (H2D of inputs, D2H of results).
     p_host = torch.from_numpy(params_np).pin_memory()
     t_host = target.cpu().pin_memory()
-    # Warm-up creates the side-stream contexts and the pinned result buffers.
+    # Warm-up creates the pipeline's streams, device buffers and pinned results.
     for _ in range(5):
         torch_layer.fused_loss(p_host, t_host, SIGMA)
     torch.cuda.synchronize(dev)
@@ -358,7 +358,9 @@ def main():
                        "l2": "flushed (256 MiB write) before every timed step"},
             "e2e": {"value": world * dense_pairs(B) / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "diffrast.torch_layer.fused_loss on pinned CPU tensors"},
+                    "api": "diffrast.torch_layer.fused_loss on pinned CPU tensors "
+                           "(dr_loss_backward_host: chunked upload, kernels and download "
+                           "in one call)"},
             "gpu_launches": 2 * args.steps,
             "roofline": {"bound": "fp32", "achieved": achieved, "peak": fp32_peak,
                          "unit": "TFLOP/s", "frac": achieved / fp32_peak,

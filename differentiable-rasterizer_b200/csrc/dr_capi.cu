@@ -98,6 +98,11 @@ struct dr_ctx {
   cudaStream_t capture_stream = nullptr;
   cudaGraphExec_t fit_exec = nullptr;
   std::vector<unsigned char> fit_key;
+  // dr_loss_backward_host: device copies of the caller's host buffers, and the
+  // streams and events of its upload / compute / download pipeline.
+  Slot io_params, io_targets, io_grads, io_losses;
+  cudaStream_t io_copy = nullptr, io_comp[2] = {nullptr, nullptr};
+  cudaEvent_t io_ev[DR_HOST_CHUNKS_MAX + 1] = {};
 
   ~dr_ctx() {}
 };
@@ -136,11 +141,16 @@ dr_status ensure(dr_ctx* c, Slot& s, size_t bytes, bool zero) {
   return DR_OK;
 }
 
+// Every scratch buffer a context owns.
+std::vector<Slot*> slots(dr_ctx* c) {
+  return {&c->recs,      &c->partials,  &c->counters, &c->bgbuf,     &c->split,
+          &c->fit_params, &c->fit_m,    &c->fit_v,    &c->fit_grads, &c->fit_losses,
+          &c->fit_state, &c->io_params, &c->io_targets, &c->io_grads, &c->io_losses};
+}
+
 uint64_t pool_bytes(dr_ctx* c) {
   uint64_t b = 0;
-  for (Slot* s : {&c->recs, &c->partials, &c->counters, &c->bgbuf, &c->split, &c->fit_params,
-                  &c->fit_m, &c->fit_v, &c->fit_grads, &c->fit_losses, &c->fit_state})
-    b += s->cap;
+  for (Slot* s : slots(c)) b += s->cap;
   return b;
 }
 
@@ -174,10 +184,10 @@ dr_status check_common(dr_ctx* ctx, const float* params, int B, int T, int H, in
   return DR_OK;
 }
 
-// Builds the shared part of the raster arguments and runs the set-up kernel.
-dr_status prepare(dr_ctx* ctx, const float* params, const float* background, int bg_per_scene,
-                  int B, int T, int H, int W, float sigma, int layout, int tape, RasterArgs& a,
-                  cudaStream_t s) {
+// The raster arguments every launch shares: sizes, sigma, precision, layout
+// and the loss normalisation (no background, records or buffers).
+void base_args(const dr_ctx* ctx, int B, int T, int H, int W, float sigma, int layout,
+               RasterArgs& a) {
   memset(&a, 0, sizeof(a));
   a.B = B;
   a.T = T;
@@ -192,6 +202,13 @@ dr_status prepare(dr_ctx* ctx, const float* params, const float* background, int
   a.layout = layout;
   a.n_values = (double)H * (double)W * 3.0;
   a.grad_scale = 2.0f / (float)((long long)H * W * 3);  // grad.rs:112
+}
+
+// Builds the shared part of the raster arguments and runs the set-up kernel.
+dr_status prepare(dr_ctx* ctx, const float* params, const float* background, int bg_per_scene,
+                  int B, int T, int H, int W, float sigma, int layout, int tape, RasterArgs& a,
+                  cudaStream_t s) {
+  base_args(ctx, B, T, H, W, sigma, layout, a);
   a.bg_per_scene = bg_per_scene ? 1 : 0;
   if (!background) {
     a.bg3[0] = a.bg3[1] = a.bg3[2] = 0.0f;
@@ -342,11 +359,13 @@ dr_status dr_ctx_destroy(dr_ctx* c) {
   {
     DeviceGuard g(c->device);
     cudaDeviceSynchronize();
-    for (Slot* s : {&c->recs, &c->partials, &c->counters, &c->bgbuf, &c->split, &c->fit_params,
-                    &c->fit_m, &c->fit_v, &c->fit_grads, &c->fit_losses, &c->fit_state})
-      free_slot(*s);
+    for (Slot* s : slots(c)) free_slot(*s);
     if (c->fit_exec) cudaGraphExecDestroy(c->fit_exec);
     if (c->capture_stream) cudaStreamDestroy(c->capture_stream);
+    for (cudaStream_t st : {c->io_copy, c->io_comp[0], c->io_comp[1]})
+      if (st) cudaStreamDestroy(st);
+    for (cudaEvent_t ev : c->io_ev)
+      if (ev) cudaEventDestroy(ev);
   }
   delete c;
   return DR_OK;
@@ -491,6 +510,142 @@ dr_status dr_triangle_block_backward(dr_ctx* ctx, const float* params, const flo
   return DR_OK;
 }
 
+int dr_host_chunks(int B, int* lo, int* hi) {
+  if (B <= 0 || !lo || !hi) return 0;
+  const double cut[DR_HOST_CHUNKS_MAX - 1] = {0.0625, 0.25, 0.5, 0.75};
+  int n = 0, prev = 0;
+  for (int i = 0; i < DR_HOST_CHUNKS_MAX; ++i) {
+    const int c = i + 1 < DR_HOST_CHUNKS_MAX ? (int)(B * cut[i] + 0.5) : B;
+    if (c > prev) {
+      lo[n] = prev;
+      hi[n] = c;
+      ++n;
+      prev = c;
+    }
+  }
+  return n;
+}
+
+dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params, const float* background,
+                                int bg_per_scene, int B, int T, int H, int W, float sigma,
+                                const float* targets, int layout, float* grads, float* losses,
+                                dr_stream_t stream) {
+  dr_status st = check_common(ctx, params, B, T, H, W, sigma, layout);
+  if (st) return st;
+  if (B > 0 && (!targets || !losses || (T > 0 && !grads)))
+    return fail(DR_INVALID_ARGUMENT, "null target, losses or grads pointer");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  if (B == 0) return DR_OK;
+  const size_t per_p = (size_t)T * kParams, per_t = (size_t)H * W * 3;
+  const int tiles = ((W + kTileSide - 1) / kTileSide) * ((H + kTileSide - 1) / kTileSide);
+  int lo[DR_HOST_CHUNKS_MAX], hi[DR_HOST_CHUNKS_MAX], k[DR_HOST_CHUNKS_MAX];
+  size_t split_at[DR_HOST_CHUNKS_MAX + 1] = {0};
+  const int nc = dr_host_chunks(B, lo, hi);
+  for (int c = 0; c < nc; ++c) {
+    const int n = hi[c] - lo[c];
+    k[c] = ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(n, T, tiles);
+    split_at[c + 1] = split_at[c] + (k[c] > 1 ? raster_split_bytes(n, k[c], H, W) : 0);
+  }
+  const bool per_scene = background && bg_per_scene;
+  if ((st = ensure(ctx, ctx->io_params, sizeof(float) * per_p * B, false))) return st;
+  if ((st = ensure(ctx, ctx->io_targets, sizeof(float) * per_t * B, false))) return st;
+  if ((st = ensure(ctx, ctx->io_grads, sizeof(float) * per_p * B, false))) return st;
+  if ((st = ensure(ctx, ctx->io_losses, sizeof(float) * (size_t)B, false))) return st;
+  if ((st = ensure(ctx, ctx->recs, tri_rec_bytes() * (size_t)B * T, false))) return st;
+  if ((st = ensure(ctx, ctx->partials, sizeof(double) * (size_t)B * tiles, false))) return st;
+  if ((st = ensure(ctx, ctx->counters, sizeof(unsigned) * (size_t)B, true))) return st;
+  if (split_at[nc] && (st = ensure(ctx, ctx->split, split_at[nc], false))) return st;
+  if (per_scene && (st = ensure(ctx, ctx->bgbuf, sizeof(float) * 3 * (size_t)B, false)))
+    return st;
+  if (!ctx->io_copy) {
+    cudaStream_t q[3] = {};
+    for (cudaStream_t& x : q)
+      DR_CUDA(cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking), "host pipeline streams");
+    for (cudaEvent_t& ev : ctx->io_ev)
+      if (!ev) DR_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "host pipeline events");
+    ctx->io_copy = q[0];
+    ctx->io_comp[0] = q[1];
+    ctx->io_comp[1] = q[2];
+  }
+  float* P = (float*)ctx->io_params.ptr;
+  float* Tg = (float*)ctx->io_targets.ptr;
+  float* G = (float*)ctx->io_grads.ptr;
+  float* L = (float*)ctx->io_losses.ptr;
+  TriRec* R = (TriRec*)ctx->recs.ptr;
+  cudaError_t err = cudaSuccess;
+  const char* where = "";
+  auto chk = [&](cudaError_t e, const char* what) {
+    if (err == cudaSuccess && e != cudaSuccess) {
+      err = e;
+      where = what;
+    }
+  };
+  // After the caller's stream's work.
+  cudaEvent_t after = ctx->io_ev[DR_HOST_CHUNKS_MAX];
+  chk(cudaEventRecord(after, (cudaStream_t)stream), "ordering after the caller's stream");
+  for (cudaStream_t q : {ctx->io_copy, ctx->io_comp[0], ctx->io_comp[1]})
+    chk(cudaStreamWaitEvent(q, after, 0), "ordering after the caller's stream");
+  if (per_scene)
+    chk(cudaMemcpyAsync(ctx->bgbuf.ptr, background, sizeof(float) * 3 * (size_t)B,
+                        cudaMemcpyHostToDevice, ctx->io_copy),
+        "uploading backgrounds");
+  // Every upload is queued first: a download into pageable memory blocks the
+  // host thread, and must not hold back later chunks' uploads.
+  for (int c = 0; c < nc; ++c) {
+    const size_t l = lo[c], n = hi[c] - lo[c];
+    chk(cudaMemcpyAsync(P + l * per_p, params + l * per_p, sizeof(float) * n * per_p,
+                        cudaMemcpyHostToDevice, ctx->io_copy),
+        "uploading parameters");
+    chk(cudaMemcpyAsync(Tg + l * per_t, targets + l * per_t, sizeof(float) * n * per_t,
+                        cudaMemcpyHostToDevice, ctx->io_copy),
+        "uploading targets");
+    chk(cudaEventRecord(ctx->io_ev[c], ctx->io_copy), "recording an upload");
+  }
+  for (int c = 0; c < nc && err == cudaSuccess; ++c) {
+    const size_t l = lo[c];
+    const int n = hi[c] - lo[c];
+    cudaStream_t q = ctx->io_comp[c & 1];
+    chk(cudaStreamWaitEvent(q, ctx->io_ev[c], 0), "waiting for an upload");
+    if (T > 0)
+      chk(cudaMemsetAsync(G + l * per_p, 0, sizeof(float) * n * per_p, q), "zeroing gradients");
+    RasterArgs a;
+    base_args(ctx, n, T, H, W, sigma, layout, a);
+    if (per_scene) {
+      a.bg_dev = (const float*)ctx->bgbuf.ptr + 3 * l;
+      a.bg_per_scene = 1;
+    } else if (background) {
+      a.bg3[0] = background[0];
+      a.bg3[1] = background[1];
+      a.bg3[2] = background[2];
+    }
+    a.recs = R + l * T;
+    chk(launch_setup(P + l * per_p, n * T, W, H, sigma, 1, R + l * T, q), "set-up kernel");
+    a.other = Tg + l * per_t;
+    a.grads = G + l * per_p;
+    a.losses = L + l;
+    a.loss_partials = (double*)ctx->partials.ptr + l * tiles;
+    a.loss_counters = (unsigned*)ctx->counters.ptr + l;
+    if (k[c] > 1)
+      chk(launch_raster_split(kModeLoss, a, tiles, k[c],
+                              (float4*)((char*)ctx->split.ptr + split_at[c]), q),
+          "split raster kernels");
+    else
+      chk(launch_raster(kModeLoss, a, tiles, q), "raster kernel");
+    if (T > 0)
+      chk(cudaMemcpyAsync(grads + l * per_p, G + l * per_p, sizeof(float) * n * per_p,
+                          cudaMemcpyDeviceToHost, q),
+          "downloading gradients");
+    chk(cudaMemcpyAsync(losses + l, L + l, sizeof(float) * n, cudaMemcpyDeviceToHost, q),
+        "downloading losses");
+  }
+  // The host buffers stay in use until every stream is done, errors included.
+  for (cudaStream_t q : {ctx->io_comp[0], ctx->io_comp[1], ctx->io_copy})
+    chk(cudaStreamSynchronize(q), "host pipeline");
+  if (err != cudaSuccess) return cuda_fail(err, where);
+  return DR_OK;
+}
+
 dr_status dr_mse_loss(dr_ctx* ctx, const float* images, const float* targets, int B,
                       int64_t n_per_image, float* losses, dr_stream_t stream) {
   if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
@@ -569,10 +724,7 @@ dr_status dr_clear_pool(dr_ctx* ctx) {
   std::lock_guard<std::mutex> lock(ctx->mu);
   DeviceGuard g(ctx->device);
   cudaDeviceSynchronize();
-  for (Slot* s : {&ctx->recs, &ctx->partials, &ctx->counters, &ctx->bgbuf, &ctx->split,
-                  &ctx->fit_params, &ctx->fit_m, &ctx->fit_v, &ctx->fit_grads, &ctx->fit_losses,
-                  &ctx->fit_state})
-    free_slot(*s);
+  for (Slot* s : slots(ctx)) free_slot(*s);
   if (ctx->fit_exec) {
     cudaGraphExecDestroy(ctx->fit_exec);
     ctx->fit_exec = nullptr;

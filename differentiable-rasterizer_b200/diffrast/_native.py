@@ -79,6 +79,8 @@ SIGNATURES = {
     "dr_set_triangle_split": (_I, [_P, _I]),
     "dr_render": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "dr_loss_backward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P, _P]),
+    "dr_loss_backward_host": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P]),
+    "dr_host_chunks": (_I, [_I, _P, _P]),
     "dr_grad_backward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P]),
     "dr_loss_backward_sharded": (
         _I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _I, _I, _P, _P, _P]),
@@ -277,78 +279,43 @@ def render(params: torch.Tensor, height: int, width: int, sigma: float, backgrou
     return out
 
 
-# Host-buffer calls: a copy stream and two compute streams per device.
-_side: dict[int, tuple] = {}
-
-
-def _side_streams(dev: torch.device):
-    s = _side.get(dev.index)
-    if s is None:
-        with _lock:
-            s = _side.get(dev.index)
-            if s is None:
-                s = (torch.cuda.Stream(device=dev),
-                     (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)))
-                _side[dev.index] = s
-    return s
+HOST_CHUNKS_MAX = 5  # DR_HOST_CHUNKS_MAX
 
 
 def host_chunks(batch: int) -> list[tuple[int, int]]:
-    """Scene ranges [lo, hi) of the pipelined host path: cuts at 1/8, 3/8, 5/8
-    and 7/8 of the batch, so the first and last chunks are half the others
-    (32 scenes: 4, 8, 8, 8, 4). The first chunk's upload and the last chunk's
-    computation overlap nothing; halving them shortens the whole call."""
-    cuts = sorted({0, batch, *(int(batch * f + 0.5) for f in (0.125, 0.375, 0.625, 0.875))})
-    return [(lo, hi) for lo, hi in zip(cuts, cuts[1:]) if hi > lo]
+    """Scene ranges [lo, hi) that dr_loss_backward_host pipelines (dr_host_chunks):
+    cuts at 1/16, 1/4, 1/2 and 3/4 of the batch (32 scenes: 2, 6, 8, 8, 8)."""
+    lo = (ctypes.c_int * HOST_CHUNKS_MAX)()
+    hi = (ctypes.c_int * HOST_CHUNKS_MAX)()
+    n = lib().dr_host_chunks(int(batch), lo, hi)
+    return [(lo[c], hi[c]) for c in range(n)]
 
 
-def _loss_backward_from_host(params: torch.Tensor, targets: torch.Tensor, sigma: float,
-                             background, layout: int, dev: torch.device):
-    """dr_loss_backward on host tensors, pipelined over scene chunks.
+def loss_backward_host(params: torch.Tensor, targets: torch.Tensor, sigma: float,
+                       background=(0.0, 0.0, 0.0), layout: int = LAYOUT_BHWC,
+                       device: torch.device | None = None):
+    """dr_loss_backward_host: host tensors in, host tensors out.
 
-    Scenes are independent, so the batch is cut into up to five chunks
-    (host_chunks). Each chunk's upload runs on a copy stream. Its kernel waits
-    only for that upload and runs on one of two compute streams, so chunk c
-    computes while chunk c + 1 uploads, and the tail of one chunk's kernel
-    overlaps the next. Results stay on the device; the caller's stream waits
-    for all chunks.
-    """
+    The library uploads the batch in scene chunks on a copy stream and runs
+    each chunk's kernels and download as soon as its upload lands. Pinned
+    inputs (``tensor.pin_memory()``) move at full PCIe rate, and the results
+    then come back in pinned tensors. Returns (losses (B,), grads (B, T, 10))."""
+    sigma = _check_sigma(sigma)
+    dev = _resolve_device(device)
     p = params.detach().to(torch.float32).contiguous()
     t = targets.detach().to(torch.float32).contiguous()
+    if p.is_cuda or t.is_cuda:
+        raise ValueError("loss_backward_host takes host tensors")
     B, T = p.shape[0], p.shape[1]
-    if layout == LAYOUT_BCHW:
-        H, W = t.shape[2], t.shape[3]
-    else:
-        H, W = t.shape[1], t.shape[2]
-    cur = torch.cuda.current_stream(dev)
-    copy_s, comp = _side_streams(dev)
-    p_d = torch.empty(p.shape, dtype=torch.float32, device=dev)
-    t_d = torch.empty(t.shape, dtype=torch.float32, device=dev)
-    grads = torch.empty((B, T, N_PARAMS), dtype=torch.float32, device=dev)
-    losses = torch.empty((B,), dtype=torch.float32, device=dev)
+    H, W = (t.shape[2], t.shape[3]) if layout == LAYOUT_BCHW else (t.shape[1], t.shape[2])
+    pin = p.is_pinned() and t.is_pinned()
+    grads = torch.empty((B, T, N_PARAMS), dtype=torch.float32, pin_memory=pin)
+    losses = torch.empty((B,), dtype=torch.float32, pin_memory=pin)
     bg, per = _bg_host(background, B)
-    # Work the caller already queued (on these buffers' memory) comes first.
-    copy_s.wait_stream(cur)
-    for s in comp:
-        s.wait_stream(cur)
-    for c, (lo, hi) in enumerate(host_chunks(B)):
-        with torch.cuda.stream(copy_s):
-            p_d[lo:hi].copy_(p[lo:hi], non_blocking=True)
-            t_d[lo:hi].copy_(t[lo:hi], non_blocking=True)
-        ready = torch.cuda.Event()
-        ready.record(copy_s)
-        s = comp[c % 2]
-        s.wait_event(ready)
-        bg_c = bg[3 * lo:3 * hi] if per else bg
-        check(lib().dr_loss_backward(context(dev, s.cuda_stream), _ptr(p_d[lo:hi]), _ptr(bg_c),
-                                     per, hi - lo, T, H, W, sigma, _ptr(t_d[lo:hi]), layout,
-                                     _ptr(grads[lo:hi]), _ptr(losses[lo:hi]), None,
-                                     ctypes.c_void_p(s.cuda_stream)))
-    for s in comp:
-        cur.wait_stream(s)
-    for buf in (p_d, t_d, grads, losses):
-        for s in (copy_s,) + comp:
-            buf.record_stream(s)
+    s = _stream(dev)
+    check(lib().dr_loss_backward_host(context(dev, s), _ptr(p), _ptr(bg), per, B, T, H, W, sigma,
+                                      _ptr(t), layout, _ptr(grads), _ptr(losses),
+                                      ctypes.c_void_p(s)))
     return losses, grads
 
 
@@ -357,13 +324,14 @@ def loss_backward(params: torch.Tensor, targets: torch.Tensor, sigma: float,
                   device: torch.device | None = None):
     """dr_loss_backward. Returns (losses (B,), grads (B,T,10)[, image]).
 
-    With host tensors (and no image requested) the upload is pipelined with
-    the computation over scene chunks (_loss_backward_from_host)."""
+    With host tensors (and no image requested) the call runs on host buffers
+    end to end (loss_backward_host, the upload pipelined with the
+    computation) and returns host tensors."""
     sigma = _check_sigma(sigma)
     dev = _resolve_device(device if device is not None else params.device)
     if (not want_image and not params.is_cuda and not targets.is_cuda and params.dim() == 3
             and params.shape[0] > 1 and params.shape[1] > 0):
-        return _loss_backward_from_host(params, targets, sigma, background, layout, dev)
+        return loss_backward_host(params, targets, sigma, background, layout, dev)
     p = _as_cuda_f32(params, dev)
     t = _as_cuda_f32(targets, dev)
     B, T = p.shape[0], p.shape[1]

@@ -225,16 +225,15 @@ def fused_loss(
             f"batch mismatch: {params.shape[0]} parameter rows but {targets.shape[0]} targets")
     if not (sigma > 0) or sigma == float("inf"):
         raise ValueError("sigma must be positive and finite")
+    if params.device.type == "cpu" and targets.device.type == "cpu":
+        # Host buffers end to end: uploads, kernels and downloads pipelined in
+        # the library (dr_loss_backward_host), one call, results in host memory.
+        losses, grads = _native.loss_backward_host(params, targets, sigma, background,
+                                                   _native.LAYOUT_BHWC)
+        _note_gpu()
+        return losses, grads.to(params.dtype)
     losses, grads = _native.loss_backward(params, targets, sigma, background, _native.LAYOUT_BHWC)
     _note_gpu()
-    if params.device.type == "cpu":
-        # One synchronisation for both results, through pinned buffers.
-        losses_h = torch.empty(losses.shape, dtype=losses.dtype, pin_memory=True)
-        grads_h = torch.empty(grads.shape, dtype=grads.dtype, pin_memory=True)
-        losses_h.copy_(losses, non_blocking=True)
-        grads_h.copy_(grads, non_blocking=True)
-        torch.cuda.current_stream(losses.device).synchronize()
-        return losses_h, grads_h.to(params.dtype)
     return losses.to(params.device), grads.to(params.device, params.dtype)
 
 

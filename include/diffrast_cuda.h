@@ -142,6 +142,33 @@ DR_API dr_status dr_loss_backward(dr_ctx* ctx, const float* params, const float*
                            const float* targets, int layout, float* grads, float* losses,
                            float* image, dr_stream_t stream);
 
+/* dr_loss_backward on HOST buffers: params, background, targets, grads and
+ * losses are all host memory (pinned memory, e.g. cudaHostAlloc'd, moves at
+ * full PCIe rate; pageable memory works, through the driver's staging). The
+ * batch is cut into scene chunks (dr_host_chunks). Every chunk's upload is
+ * queued on a copy stream first; each chunk's set-up, raster launch and
+ * download then run on one of two compute streams as soon as its upload
+ * lands, so uploads, kernels and downloads overlap. The call returns when
+ * grads and losses are in host memory (the work is ordered after `stream`).
+ * Same results as dr_loss_backward. Replaces the host-array path of
+ * diffrast_rs.fused_loss_backward (diffrast-py/src/lib.rs:331-412: numpy in,
+ * numpy out) and GpuRasterizer::backward_many's upload / readback
+ * (diffrast-gpu/src/lib.rs:639-816). */
+DR_API dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params,
+                                       const float* background, int bg_per_scene, int B, int T,
+                                       int H, int W, float sigma, const float* targets,
+                                       int layout, float* grads, float* losses,
+                                       dr_stream_t stream);
+
+/* The scene chunks dr_loss_backward_host cuts a batch of B into: chunk c is
+ * scenes [lo[c], hi[c]). Cuts fall at 1/16, 1/4, 1/2 and 3/4 of the batch: the
+ * first chunk, whose upload overlaps nothing, is small, and the others are
+ * large enough for their kernels to keep up with the uploads. 32 scenes go as
+ * 2, 6, 8, 8, 8. lo and hi hold DR_HOST_CHUNKS_MAX entries. Returns the number
+ * of chunks (0 for B <= 0). */
+#define DR_HOST_CHUNKS_MAX 5
+DR_API int dr_host_chunks(int B, int* lo, int* hi);
+
 /* Backward from an upstream image gradient dL/d(image) (same layout rules).
  * grads (B,T,10) is overwritten. Replaces GpuRasterizer::backward_many_from_grad
  * (diffrast-gpu/src/lib.rs:828-910) and diffrast_rs.backward_batch

@@ -31,7 +31,8 @@ def test_header_declares_the_entry_points():
     names = declared_symbols()
     for required in ("dr_ctx_create", "dr_render", "dr_loss_backward", "dr_grad_backward",
                      "dr_mse_loss", "dr_adam_step", "dr_fit", "dr_loss_backward_sharded",
-                     "dr_triangle_block_forward", "dr_triangle_block_backward"):
+                     "dr_triangle_block_forward", "dr_triangle_block_backward",
+                     "dr_loss_backward_host", "dr_host_chunks"):
         assert required in names
 
 
@@ -90,15 +91,19 @@ def test_argument_errors_need_no_device():
                                        None) == _native.INVALID_ARGUMENT
     assert L.dr_triangle_block_backward(None, None, None, 0, 1, 1, 8, 8, 0.01, 2, 1, None, None, 0,
                                         0, None, None, None, None) == _native.INVALID_ARGUMENT
+    assert L.dr_loss_backward_host(None, None, None, 0, 1, 1, 8, 8, 0.01, None, 0, None, None,
+                                   None) == _native.INVALID_ARGUMENT
 
 
 def test_host_chunks_cover_the_batch_in_order():
+    # dr_host_chunks is pure host logic: callable without a GPU.
     from diffrast._native import host_chunks
 
+    assert host_chunks(0) == [] and host_chunks(1) == [(0, 1)]
     for b in range(2, 130):
         ch = host_chunks(b)
         assert ch[0][0] == 0 and ch[-1][1] == b
         assert all(lo < hi for lo, hi in ch)
         assert all(ch[i][1] == ch[i + 1][0] for i in range(len(ch) - 1))
         assert len(ch) <= 5
-    assert [hi - lo for lo, hi in host_chunks(32)] == [4, 8, 8, 8, 4]
+    assert [hi - lo for lo, hi in host_chunks(32)] == [2, 6, 8, 8, 8]

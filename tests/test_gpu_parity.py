@@ -367,7 +367,8 @@ def test_fast_mode_tracks_the_exact_gradient(native, oracle, size, T, sigma):
 
 @pytest.mark.parametrize("B,per_scene_bg,layout", [(7, False, 0), (32, True, 0), (5, True, 1)])
 def test_host_buffers_pipelined_equal_device_path(native, B, per_scene_bg, layout):
-    # Host tensors take the chunked upload/compute pipeline; results equal the
+    # Host tensors take the library's chunked upload/compute/download pipeline
+    # (dr_loss_backward_host) and come back as host tensors; results equal the
     # device-tensor call. Chunks of a few scenes may take the triangle split
     # while the whole batch does not, so the two agree to rounding.
     from diffrast.scenes import uniform_scenes
@@ -380,10 +381,15 @@ def test_host_buffers_pipelined_equal_device_path(native, B, per_scene_bg, layou
     bg = (torch.rand(B, 3, generator=torch.Generator().manual_seed(2)) if per_scene_bg
           else (0.1, 0.2, 0.3))
     l_h, g_h = native.loss_backward(p, tgt, 0.004, bg, layout=layout)
+    assert not l_h.is_cuda and not g_h.is_cuda and l_h.is_pinned() and g_h.is_pinned()
     l_d, g_d = native.loss_backward(p.cuda(), tgt.cuda(), 0.004, bg, layout=layout)
-    torch.cuda.synchronize()
-    torch.testing.assert_close(l_h, l_d, rtol=1e-6, atol=0)
+    torch.testing.assert_close(l_h, l_d.cpu(), rtol=1e-6, atol=0)
     assert_grads_close(host(g_h), host(g_d), "host pipeline")
+    # Pageable buffers take the same path through the driver's staging.
+    l_p, g_p = native.loss_backward_host(p.clone(), tgt.clone(), 0.004, bg, layout=layout)
+    assert not l_p.is_pinned()
+    torch.testing.assert_close(l_p, l_h, rtol=0, atol=0)
+    assert_grads_close(host(g_p), host(g_h), "pageable host buffers")
 
 
 @pytest.fixture(params=[1, 2, 3, 8])
