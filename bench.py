@@ -67,17 +67,9 @@ def dense_pairs(batch: int) -> int:
 
 def bbox_pairs(params: np.ndarray) -> int:
     """Bounding-box pairs (raster.rs:144-168 boxes of live triangles)."""
-    import oracle
+    from diffrast.scenes import bbox_pairs as count
 
-    n = 0
-    for b in range(params.shape[0]):
-        for k in range(params.shape[1]):
-            if not (params[b, k, 9] > 0):
-                continue
-            bb = oracle.pixel_bounds(params[b, k], W, H, SIGMA)
-            if bb:
-                n += (bb[2] - bb[0]) * (bb[3] - bb[1])
-    return n
+    return count(params, W, H, SIGMA)
 
 
 def inputs(rank: int):
@@ -168,15 +160,18 @@ def fit_metric(dev, with_cpu: bool):
     defaults), the whole loop on the device (dr_fit, one CUDA graph)."""
     import torch
 
-    import oracle
     from diffrast import _native
+    from diffrast.fit import mean_color, seed_colors
     from diffrast.scenes import config1_target_scene, seed_scene_geometry
 
-    oracle.build()
-    target = oracle.render_batch(config1_target_scene(150, 0), 176, 176, 0.0015)[0]
+    # The target is rendered by this library; the initial scene follows
+    # fit.rs:356-385 (seed_colors / mean_color).
+    t_dev = _native.render(torch.from_numpy(config1_target_scene(150, 0)).to(dev), 176, 176,
+                           0.0015)[0].contiguous()
+    target = t_dev.cpu().numpy()
     p = seed_scene_geometry(150, 1)
-    bg = oracle.seed_colors(target, p)
-    t_dev = torch.from_numpy(target).to(dev)
+    seed_colors(target, p)
+    bg = mean_color(target)
     p_dev = torch.from_numpy(p).to(dev)
     kw = dict(iters=800, patience=None)
     _native.fit(t_dev, p_dev, [float(v) for v in bg], **kw)  # capture + warm-up
@@ -196,6 +191,9 @@ def fit_metric(dev, with_cpu: bool):
            "timing": "CUDA events around dr_fit (one graph launch per 800-iteration fit)",
            "final_best_loss": rep["best_loss"]}
     if with_cpu:
+        import oracle
+
+        oracle.build()
         t0 = time.perf_counter()
         r = oracle.fit(target, p, bg, oracle.FitConfig(iters=200, patience=None))
         cdt = time.perf_counter() - t0

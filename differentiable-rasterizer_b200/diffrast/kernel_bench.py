@@ -12,6 +12,10 @@ and achieved GB/s against the measured HBM peak. All sizes are far above the
 
 The first call of each is the measured size, so an ncu capture of the first
 launch of each kernel (``-c 3``) sees the same work.
+
+``--fit-iters N`` instead runs the config 1 fit (150 triangles, 176x176) for
+N iterations through ``dr_fit`` (one CUDA graph) twice, and prints the second
+run's time per iteration: a short driver for the fit graph's launch list.
 """
 
 from __future__ import annotations
@@ -52,7 +56,11 @@ def _time(fn, reps: int) -> float:
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--fit-iters", type=int, default=0)
     args = ap.parse_args(argv)
+    if args.fit_iters > 0:
+        fit_graph(args.fit_iters)
+        return
     peak, src = _peak_gbs()
     g = torch.Generator(device="cuda").manual_seed(0)
 
@@ -87,6 +95,27 @@ def main(argv=None) -> None:
 
     ms = _time(adam, args.reps)
     line("dr_adam_kernel", 28 * npar, ms, f"{npar} parameters")
+
+
+def fit_graph(iters: int) -> None:
+    from .fit import mean_color, seed_colors
+    from .scenes import config1_target_scene, seed_scene_geometry
+
+    target = _native.render(torch.from_numpy(config1_target_scene(150, 0)).cuda(), 176, 176,
+                            0.0015)[0].contiguous()
+    p = seed_scene_geometry(150, 1)
+    seed_colors(target.cpu().numpy(), p)
+    bg = [float(x) for x in mean_color(target.cpu().numpy())]
+    p_dev = torch.from_numpy(p).cuda()
+    _native.fit(target, p_dev, bg, iters=iters, patience=None)  # capture
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    _native.fit(target, p_dev, bg, iters=iters, patience=None)
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"fit": "config 1", "iters": iters,
+                      "us_per_iter": e0.elapsed_time(e1) * 1e3 / iters}), flush=True)
 
 
 if __name__ == "__main__":

@@ -109,3 +109,26 @@ def config5_params(batch: int = 16, tris: int = 2048, seed: int = 5000) -> np.nd
         p[idx[n_deg + n_a:n_deg + 2 * n_a], 9] = 1.0
         out[b] = p
     return out
+
+
+def bbox_pairs(params: np.ndarray, width: int, height: int, sigma: float) -> int:
+    """Bounding-box pairs of a batch, the roofline's unit of work: the pixels
+    inside pixel_bounds (raster.rs:144-168, f32 arithmetic: 6 sigma of padding,
+    floor / ceil + 1, clamped to the canvas) summed over the triangles with
+    alpha > 0 and finite vertices."""
+    p = np.asarray(params, dtype=np.float32).reshape(-1, 10)
+    v = p[:, :6].reshape(-1, 3, 2)
+    live = (p[:, 9] > 0) & np.isfinite(v).all(axis=(1, 2))
+    v = v[live]
+    if v.shape[0] == 0:
+        return 0
+    pad = np.float32(6.0) * np.float32(sigma)
+    size = np.array([width, height], dtype=np.float32)
+    lo = np.floor((v.min(axis=1) - pad) * size)
+    hi = np.ceil((v.max(axis=1) + pad) * size)
+    lim = np.float32(2.0 ** 62)  # far beyond any canvas: saturation is never reached
+    x0y0 = np.minimum(np.maximum(lo, 0), lim).astype(np.int64)
+    x1y1 = np.minimum(np.minimum(np.maximum(hi, 0), lim).astype(np.int64) + 1,
+                      np.array([width, height], dtype=np.int64))
+    ext = np.clip(x1y1 - x0y0, 0, None)
+    return int((ext[:, 0] * ext[:, 1]).sum())

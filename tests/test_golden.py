@@ -104,3 +104,24 @@ def test_cuda_matches_golden(name):
     ref_l = z[f"{name}/losses"]
     np.testing.assert_allclose(losses.cpu().numpy(), ref_l, rtol=1e-5, atol=1e-12)
     assert_grads_close(grads.cpu().numpy(), z[f"{name}/grads"], f"{name} grads")
+
+
+def test_bbox_pair_count_matches_the_oracle_boxes(oracle):
+    # The roofline's unit of work, counted on the host with numpy, against the
+    # oracle's pixel_bounds (raster.rs:144-168) triangle by triangle.
+    from diffrast.scenes import bbox_pairs, config5_params, uniform_scenes
+
+    rng = np.random.default_rng(12)
+    p = np.concatenate([uniform_scenes(3, 40, 9), config5_params(2, 40, 5300)], axis=0)
+    p[0, :5, :6] = rng.uniform(-0.5, 1.5, (5, 6))  # partly or wholly off the canvas
+    p[1, 3, 0] = np.nan
+    p[1, 4, 9] = 0.0
+    for (w, h, sigma) in ((256, 256, 0.0015), (37, 45, 0.02), (1, 1, 0.0)):
+        want = 0
+        for tri in p.reshape(-1, 10):
+            if not (tri[9] > 0):
+                continue
+            bb = oracle.pixel_bounds(tri, w, h, sigma)
+            if bb:
+                want += (bb[2] - bb[0]) * (bb[3] - bb[1])
+        assert bbox_pairs(p, w, h, sigma) == want, (w, h, sigma)
