@@ -1559,25 +1559,39 @@ __global__ void dr_adam4_kernel(AdamArgs a) {
 // dr_fit's Adam step (the per-element update of dr_adam_kernel) fused with
 // the next iteration's set-up: one thread per triangle updates its 10
 // parameters, clears their gradients for the next raster launch and writes
-// the triangle's record from the updated parameters.
+// the triangle's record from the updated parameters. Every load is issued
+// before any store (the arrays could alias as far as the compiler knows), so
+// the thread waits for memory once rather than once per parameter.
 __global__ void __launch_bounds__(kSetupThreads) dr_fit_adam_setup_kernel(
     AdamArgs a, float* __restrict__ grads, int T, int W, int H, float next_sigma,
     TriRec* __restrict__ recs) {
   const int t = blockIdx.x * kSetupThreads + (int)threadIdx.x;
   if (t >= T) return;
   const long long base = (long long)t * kParams;
-  if (a.copy_flag && *a.copy_flag)
-    for (int j = 0; j < kParams; ++j) a.copy_dst[base + j] = a.params[base + j];
-  if (a.run_flag && !*a.run_flag) return;
-  for (int j = 0; j < kParams; ++j) {
-    const long long i = base + j;
-    float m = a.m[i], v = a.v[i];
-    a.params[i] = adam_one(a, i, a.params[i], grads[i], m, v);
-    a.m[i] = m;
-    a.v[i] = v;
-    grads[i] = 0.0f;
+  float p[kParams], m[kParams], v[kParams], g[kParams];
+#pragma unroll
+  for (int j = 0; j < kParams; ++j) p[j] = a.params[base + j];
+  if (a.copy_flag && *a.copy_flag) {
+#pragma unroll
+    for (int j = 0; j < kParams; ++j) a.copy_dst[base + j] = p[j];
   }
-  if (recs) recs[t] = make_record(a.params, t, W, H, next_sigma, 1);
+  if (a.run_flag && !*a.run_flag) return;
+#pragma unroll
+  for (int j = 0; j < kParams; ++j) {
+    m[j] = a.m[base + j];
+    v[j] = a.v[base + j];
+    g[j] = grads[base + j];
+  }
+#pragma unroll
+  for (int j = 0; j < kParams; ++j) p[j] = adam_one(a, base + j, p[j], g[j], m[j], v[j]);
+#pragma unroll
+  for (int j = 0; j < kParams; ++j) {
+    a.params[base + j] = p[j];
+    a.m[base + j] = m[j];
+    a.v[base + j] = v[j];
+    grads[base + j] = 0.0f;
+  }
+  if (recs) recs[t] = make_record(p, 0, W, H, next_sigma, 1);
 }
 
 // ---------------------------------------------------------------------------
