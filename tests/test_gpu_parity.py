@@ -392,6 +392,24 @@ def test_host_buffers_pipelined_equal_device_path(native, B, per_scene_bg, layou
     assert_grads_close(host(g_p), host(g_h), "pageable host buffers")
 
 
+@pytest.mark.parametrize("B,T", [(1, 40), (3, 0), (2, 130)])
+def test_host_buffers_single_scene_empty_and_long_lists(native, B, T):
+    # dr_loss_backward_host on one scene (one chunk, which may take the
+    # triangle split), on scenes without triangles (loss of the background
+    # alone), and on lists longer than one binning chunk (tile kernel).
+    from diffrast.scenes import uniform_scenes
+
+    p = torch.from_numpy(uniform_scenes(B, T, 21)).pin_memory() if T else \
+        torch.zeros(B, 0, 10).pin_memory()
+    tgt = torch.rand(B, 33, 47, 3, generator=torch.Generator().manual_seed(3)).pin_memory()
+    l_h, g_h = native.loss_backward_host(p, tgt, 0.004, (0.3, 0.2, 0.1))
+    l_d, g_d = native.loss_backward(p.cuda(), tgt.cuda(), 0.004, (0.3, 0.2, 0.1))
+    torch.testing.assert_close(l_h, l_d.cpu(), rtol=1e-6, atol=0)
+    assert g_h.shape == (B, T, 10)
+    if T:
+        assert_grads_close(host(g_h), host(g_d), "host buffers")
+
+
 @pytest.fixture(params=[1, 2, 3, 8])
 def split(native, request):
     native.set_triangle_split(request.param)
