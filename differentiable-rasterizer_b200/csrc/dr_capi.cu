@@ -559,11 +559,18 @@ dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params, const float* b
   if (per_scene && (st = ensure(ctx, ctx->bgbuf, sizeof(float) * 3 * (size_t)B, false)))
     return st;
   if (!ctx->io_copy) {
+    // Created once per context; on a failure nothing half-made is kept.
     cudaStream_t q[3] = {};
+    cudaError_t e = cudaSuccess;
     for (cudaStream_t& x : q)
-      DR_CUDA(cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking), "host pipeline streams");
+      if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking);
     for (cudaEvent_t& ev : ctx->io_ev)
-      if (!ev) DR_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "host pipeline events");
+      if (e == cudaSuccess && !ev) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+      for (cudaStream_t x : q)
+        if (x) cudaStreamDestroy(x);
+      return cuda_fail(e, "creating the host pipeline's streams and events");
+    }
     ctx->io_copy = q[0];
     ctx->io_comp[0] = q[1];
     ctx->io_comp[1] = q[2];
