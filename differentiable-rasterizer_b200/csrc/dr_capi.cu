@@ -405,6 +405,17 @@ dr_status dr_set_precision(dr_ctx* ctx, int precision) {
   return DR_OK;
 }
 
+dr_status dr_query_path(dr_ctx* ctx, int B, int T, int H, int W, int* path) {
+  if (!ctx || !path) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  if (B < 0 || T < 0 || H <= 0 || W <= 0) return fail(DR_INVALID_ARGUMENT, "bad sizes");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  const int tiles_x = (W + kTileSide - 1) / kTileSide, tiles_y = (H + kTileSide - 1) / kTileSide;
+  const int k = ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(B, T, tiles_x * tiles_y);
+  *path = raster_path(B, T, tiles_x, tiles_y, k);
+  return DR_OK;
+}
+
 dr_status dr_render(dr_ctx* ctx, const float* params, const float* background, int bg_per_scene,
                     int B, int T, int H, int W, float sigma, int layout, float* image,
                     dr_stream_t stream) {

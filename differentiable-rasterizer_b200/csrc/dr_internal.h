@@ -97,6 +97,9 @@ size_t tri_rec_bytes();
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
                          int tape_semantics, TriRec* recs, cudaStream_t s);
 cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s);
+// Which kernel a launch over B scenes of tiles_x x tile_rows tiles takes:
+// 0 the tile kernel, 1 the region kernel, 2 the triangle-block split (split_k > 1).
+int raster_path(int B, int T, int tiles_x, int tile_rows, int split_k);
 // Triangle blocks for a loss/grad launch over all tile rows of B scenes: 1 when
 // the plain launch fills the GPU, else up to 8 (at least 32 triangles each).
 int raster_split_blocks(int B, int T, int n_tiles);

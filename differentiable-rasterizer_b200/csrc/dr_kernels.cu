@@ -1673,13 +1673,23 @@ static int device_sms() {
 // the last ones finished. Halving the unit halves that tail; the list is
 // binned twice as often, for about 2 % more work.
 constexpr int kRegionRows = 1;
+static long long region_ctas(int B, int tiles_x, int tile_rows) {
+  return (long long)((tiles_x + kRegionCols - 1) / kRegionCols) *
+         ((tile_rows + kRegionRows - 1) / kRegionRows) * B;
+}
+static bool use_region_kernel(int B, int T, int tiles_x, int tile_rows) {
+  return T <= kChunk && region_ctas(B, tiles_x, tile_rows) >= 4LL * device_sms();
+}
+int raster_path(int B, int T, int tiles_x, int tile_rows, int split_k) {
+  if (split_k > 1) return 2;
+  return use_region_kernel(B, T, tiles_x, tile_rows) ? 1 : 0;
+}
 template <int Mode, int kPrec>
 static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
   constexpr int kRows = kRegionRows;
   constexpr int kRB = kRegionCols * kRows * kBlocksPerTile;
-  const long long n_ctas = (long long)((a.tiles_x + kRegionCols - 1) / kRegionCols) *
-                           ((a.tile_rows + kRows - 1) / kRows) * a.B;
-  if (a.T <= kChunk && n_ctas >= 4LL * device_sms()) {
+  const long long n_ctas = region_ctas(a.B, a.tiles_x, a.tile_rows);
+  if (use_region_kernel(a.B, a.T, a.tiles_x, a.tile_rows)) {
     if (n_ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     dr_raster_region_kernel<Mode, kPrec, kRows>
         <<<(unsigned)n_ctas, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);

@@ -21,6 +21,7 @@ LIB_PATH = os.path.join(_HERE, "libdiffrast_cuda.so")
 # dr_status (include/diffrast_cuda.h)
 OK, INVALID_ARGUMENT, TOO_LARGE, NO_DEVICE, TIMEOUT, LAUNCH, COMM, OUT_OF_MEMORY, INTERNAL = range(9)
 LAYOUT_BHWC, LAYOUT_BCHW = 0, 1
+PATH_TILE, PATH_REGION, PATH_SPLIT = 0, 1, 2  # dr_path
 STOP_COMPLETED, STOP_CONVERGED, STOP_DIVERGED = 0, 1, 2
 N_PARAMS = 10
 
@@ -77,6 +78,7 @@ SIGNATURES = {
     "dr_set_background_location": (_I, [_P, _I]),
     "dr_set_precision": (_I, [_P, _I]),
     "dr_set_triangle_split": (_I, [_P, _I]),
+    "dr_query_path": (_I, [_P, _I, _I, _I, _I, ctypes.POINTER(_I)]),
     "dr_render": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P, _P]),
     "dr_loss_backward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P, _P]),
     "dr_loss_backward_host": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P]),
@@ -201,6 +203,16 @@ def set_triangle_split(blocks: int) -> None:
     with _lock:
         for h in _ctxs.values():
             check(lib().dr_set_triangle_split(h, _split))
+
+
+def query_path(B: int, T: int, height: int, width: int,
+               device: torch.device | None = None) -> int:
+    """dr_query_path: the kernel a loss/gradient call of this shape takes
+    (PATH_TILE, PATH_REGION or PATH_SPLIT)."""
+    dev = _resolve_device(device)
+    out = ctypes.c_int(-1)
+    check(lib().dr_query_path(context(dev, _stream(dev)), B, T, height, width, ctypes.byref(out)))
+    return out.value
 
 
 def shutdown() -> bool:

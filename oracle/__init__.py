@@ -97,6 +97,11 @@ def lib():
                 [_F, _I, _I, _F, _F, _I, ctypes.POINTER(FitConfigC), _F, _I64, _F, _F, _I64, _F,
                  ctypes.POINTER(ctypes.c_int)],
             ),
+            "oracle64_fit": (
+                _I,
+                [_F, _I, _I, _F, _F, _I, ctypes.POINTER(FitConfigC), _D, _I64, _D, _D, _I64, _D,
+                 ctypes.POINTER(ctypes.c_int)],
+            ),
             "oracle_num_threads": (_I, []),
         }
         for name, (res, args) in sig.items():
@@ -312,24 +317,30 @@ class FitReport:
     stop_reason: int
 
 
-def fit(target, init_params, background, cfg: FitConfig) -> FitReport:
-    """fit.rs:166-181 from a given seeded scene; raises ValueError(ConfigError)."""
+def fit(target, init_params, background, cfg: FitConfig, f64: bool = False) -> FitReport:
+    """fit.rs:166-181 from a given seeded scene; raises ValueError(ConfigError).
+
+    ``f64=True`` runs the twin that carries parameters, Adam moments and the
+    loss in f64 (the sigma schedule and box cull stay f32): the spread between
+    the two is the f32 rounding noise floor of a fit."""
     t = _f32(target)
     H, W = t.shape[0], t.shape[1]
     p = _f32(init_params).reshape(-1, 10)
     T = p.shape[0]
     bg = _f32(background).reshape(3)
-    losses = np.zeros(max(cfg.iters, 1), dtype=np.float32)
+    dt = np.float64 if f64 else np.float32
+    losses = np.zeros(max(cfg.iters, 1), dtype=dt)
     n_losses = ctypes.c_int64(0)
-    best = np.zeros_like(p)
-    final = np.zeros_like(p)
+    best = np.zeros(p.shape, dtype=dt)
+    final = np.zeros(p.shape, dtype=dt)
     bi = ctypes.c_int64(0)
-    bl = ctypes.c_float(0)
+    bl = ctypes.c_double(0) if f64 else ctypes.c_float(0)
     stop = ctypes.c_int(0)
     c = cfg.c()
-    err = lib().oracle_fit(_p(t), H, W, _p(p), _p(bg), T, ctypes.byref(c), _p(losses),
-                           ctypes.byref(n_losses), _p(best), _p(final), ctypes.byref(bi),
-                           ctypes.byref(bl), ctypes.byref(stop))
+    fn = lib().oracle64_fit if f64 else lib().oracle_fit
+    err = fn(_p(t), H, W, _p(p), _p(bg), T, ctypes.byref(c), _p(losses),
+             ctypes.byref(n_losses), _p(best), _p(final), ctypes.byref(bi),
+             ctypes.byref(bl), ctypes.byref(stop))
     if err:
         raise ValueError(CONFIG_ERRORS[err])
     return FitReport(losses[: n_losses.value].copy(), best, final, bi.value, bl.value, stop.value)

@@ -56,13 +56,15 @@ template <typename F> struct Tri {
   float raw_v[3][2];  // the f32 vertices, for the f32 bbox cull
 };
 
-template <typename F> Tri<F> load_tri(const float* p) {
+// P is the storage type of the parameters: f32 for every entry point, f64
+// only for the f64 fit twin, whose box cull still takes the f32 vertices.
+template <typename F, typename P = float> Tri<F> load_tri(const P* p) {
   Tri<F> t;
   for (int i = 0; i < 3; ++i) {
     t.v[i][0] = (F)p[2 * i];
     t.v[i][1] = (F)p[2 * i + 1];
-    t.raw_v[i][0] = p[2 * i];
-    t.raw_v[i][1] = p[2 * i + 1];
+    t.raw_v[i][0] = (float)p[2 * i];
+    t.raw_v[i][1] = (float)p[2 * i + 1];
   }
   for (int c = 0; c < 3; ++c) t.color[c] = (F)p[6 + c];
   t.alpha = (F)p[9];
@@ -347,12 +349,12 @@ enum GradMode {
 
 // One scene: render_with_tape + backward (grad.rs:98-131), with the d_canvas
 // seeding chosen by `mode`. Writes T*10 grads, returns the loss as F.
-template <typename F>
-F scene_backward(const float* params, int T, const float bg[3], size_t W, size_t H, F sigma,
+template <typename F, typename P = float>
+F scene_backward(const P* params, int T, const float bg[3], size_t W, size_t H, F sigma,
                  const float* other, int mode, F* grads, F* image_out) {
   std::vector<Tri<F>> tris;
   tris.reserve(T);
-  for (int k = 0; k < T; ++k) tris.push_back(load_tri<F>(params + (size_t)k * kParams));
+  for (int k = 0; k < T; ++k) tris.push_back(load_tri<F, P>(params + (size_t)k * kParams));
   F bgf[3] = {(F)bg[0], (F)bg[1], (F)bg[2]};
   Canvas<F> rendered(W, H, bgf);
   std::vector<Patch<F>> tape;
@@ -636,29 +638,47 @@ int oracle_fit_validate(const OracleFitConfig* c, int T) {
   return 0;
 }
 
-// fit.rs:166-181 + Fitter::new/step (fit.rs:214-288), starting from the given
-// seeded scene (params (T,10) + background). Returns the ConfigError code (or
-// 0). Outputs: losses[iters] (n_losses filled), best_params (T,10),
-// final_params (T,10), best_iter, best_loss, stop_reason (0 Completed,
-// 1 Converged, 2 Diverged).
-int oracle_fit(const float* target, int H, int W, const float* init_params, const float* bg,
-               int T, const OracleFitConfig* cfg, float* losses, int64_t* n_losses,
-               float* best_params, float* final_params, int64_t* best_iter, float* best_loss,
-               int* stop_reason) {
+}  // extern "C"
+
+namespace {
+
+// powi in the arithmetic type F: the f32 square-and-multiply of powi_f32 for
+// F = float, the same loop in f64 for the twin.
+template <typename F> F powi_t(F a, int b) {
+  bool recip = b < 0;
+  F r = (F)1;
+  for (;;) {
+    if (b & 1) r *= a;
+    b /= 2;
+    if (b == 0) break;
+    a *= a;
+  }
+  return recip ? (F)1 / r : r;
+}
+
+// fit.rs:166-181 + Fitter::new/step (fit.rs:214-288) in the arithmetic type F.
+// F = float is the reference; F = double keeps the reference's discrete steps
+// (the sigma schedule and box cull in f32) and carries parameters, moments and
+// the loss in f64, which measures how far f32 rounding moves a fit.
+template <typename F>
+int fit_t(const float* target, int H, int W, const float* init_params, const float* bg, int T,
+          const OracleFitConfig* cfg, F* losses, int64_t* n_losses, F* best_params,
+          F* final_params, int64_t* best_iter, F* best_loss, int* stop_reason) {
   int err = oracle_fit_validate(cfg, T);
   if (err) return err;
   size_t np = (size_t)T * kParams;
-  size_t n = (size_t)H * W * 3;
-  std::vector<float> params(init_params, init_params + np), best(params), m(np, 0.0f),
-      v(np, 0.0f), lr(np), grads(np);
+  std::vector<F> params(np), m(np, (F)0), v(np, (F)0), lr(np), grads(np);
+  for (size_t i = 0; i < np; ++i) params[i] = (F)init_params[i];
+  std::vector<F> best(params);
   for (int k = 0; k < T; ++k) {  // fit.rs:388-396
-    for (int i = 0; i < 6; ++i) lr[k * kParams + i] = cfg->lr_pos;
-    for (int i = 6; i < 9; ++i) lr[k * kParams + i] = cfg->lr_color;
-    lr[k * kParams + 9] = cfg->lr_alpha;
+    for (int i = 0; i < 6; ++i) lr[k * kParams + i] = (F)cfg->lr_pos;
+    for (int i = 6; i < 9; ++i) lr[k * kParams + i] = (F)cfg->lr_color;
+    lr[k * kParams + 9] = (F)cfg->lr_alpha;
   }
+  const F beta1 = (F)0.9f, beta2 = (F)0.999f, eps = (F)1e-8f, min_delta = (F)cfg->min_delta;
   uint32_t t = 0;
   int64_t iter = 0, since = 0, bi = 0, count = 0;
-  float bl = INFINITY;
+  F bl = std::numeric_limits<F>::infinity();
   int stop = 0;
   for (;;) {
     if (iter >= cfg->iters) {
@@ -666,15 +686,15 @@ int oracle_fit(const float* target, int H, int W, const float* init_params, cons
       break;
     }
     int64_t i = iter;
-    float sigma = oracle_sigma_at(cfg->sigma_start, cfg->sigma_end, cfg->iters, i);
-    float loss = scene_backward<float>(params.data(), T, bg, W, H, sigma, target, kTarget,
-                                       grads.data(), nullptr);
+    F sigma = (F)oracle_sigma_at(cfg->sigma_start, cfg->sigma_end, cfg->iters, i);
+    F loss = scene_backward<F, F>(params.data(), T, bg, W, H, sigma, target, kTarget,
+                                  grads.data(), nullptr);
     if (!std::isfinite(loss)) {
       stop = 2;
       break;
     }
     losses[count++] = loss;
-    if (loss + cfg->min_delta < bl) {
+    if (loss + min_delta < bl) {  // fit.rs:268-275
       bl = loss;
       bi = i;
       best = params;
@@ -687,18 +707,61 @@ int oracle_fit(const float* target, int H, int W, const float* init_params, cons
       stop = 1;
       break;
     }
-    oracle_adam_step(params.data(), m.data(), v.data(), grads.data(), lr.data(), (int64_t)np, &t,
-                     0.9f, 0.999f, 1e-8f);
-    oracle_project(params.data(), T);
+    // optim.rs:40-60
+    t += 1;
+    F bc1 = (F)1 - powi_t<F>(beta1, (int)t);
+    F bc2 = (F)1 - powi_t<F>(beta2, (int)t);
+    for (size_t j = 0; j < np; ++j) {
+      F g = grads[j];
+      m[j] = beta1 * m[j] + ((F)1 - beta1) * g;
+      v[j] = beta2 * v[j] + ((F)1 - beta2) * g * g;
+      F m_hat = m[j] / bc1;
+      F v_hat = v[j] / bc2;
+      params[j] -= lr[j] * m_hat / (std::sqrt(v_hat) + eps);
+    }
+    // fit.rs:399-424
+    for (int k = 0; k < T; ++k) {
+      F* tri = params.data() + (size_t)k * kParams;
+      for (int q = 0; q < kParams; ++q)
+        if (std::isnan(tri[q])) tri[q] = (F)0.5f;
+      for (int q = 0; q < 6; ++q) tri[q] = rclamp(tri[q], (F)-0.25f, (F)1.25f);
+      for (int q = 6; q < 9; ++q) tri[q] = rclamp(tri[q], (F)0, (F)1);
+      tri[9] = rclamp(tri[9], (F)1e-3f, (F)0.999f);
+    }
   }
-  (void)n;
   *n_losses = count;
-  std::memcpy(best_params, best.data(), np * sizeof(float));
-  std::memcpy(final_params, params.data(), np * sizeof(float));
+  std::memcpy(best_params, best.data(), np * sizeof(F));
+  std::memcpy(final_params, params.data(), np * sizeof(F));
   *best_iter = bi;
   *best_loss = bl;
   *stop_reason = stop;
   return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+// fit.rs:166-181 + Fitter::new/step (fit.rs:214-288), starting from the given
+// seeded scene (params (T,10) + background). Returns the ConfigError code (or
+// 0). Outputs: losses[iters] (n_losses filled), best_params (T,10),
+// final_params (T,10), best_iter, best_loss, stop_reason (0 Completed,
+// 1 Converged, 2 Diverged).
+int oracle_fit(const float* target, int H, int W, const float* init_params, const float* bg,
+               int T, const OracleFitConfig* cfg, float* losses, int64_t* n_losses,
+               float* best_params, float* final_params, int64_t* best_iter, float* best_loss,
+               int* stop_reason) {
+  return fit_t<float>(target, H, W, init_params, bg, T, cfg, losses, n_losses, best_params,
+                      final_params, best_iter, best_loss, stop_reason);
+}
+
+// The same fit with f64 parameters, moments and loss (the noise-floor twin).
+int oracle64_fit(const float* target, int H, int W, const float* init_params, const float* bg,
+                 int T, const OracleFitConfig* cfg, double* losses, int64_t* n_losses,
+                 double* best_params, double* final_params, int64_t* best_iter,
+                 double* best_loss, int* stop_reason) {
+  return fit_t<double>(target, H, W, init_params, bg, T, cfg, losses, n_losses, best_params,
+                       final_params, best_iter, best_loss, stop_reason);
 }
 
 int oracle_num_threads(void) { return clamp_threads(0); }

@@ -413,3 +413,23 @@ def test_gradient_input_modes_agree(oracle):
     norm = np.linalg.norm(via_target)
     assert np.max(np.abs(inv - via_target)) / norm < 1e-3
     assert np.max(np.abs(direct - via_target)) / norm < 1e-4
+
+
+def test_f64_fit_twin_tracks_the_f32_fit(oracle):
+    # The f64 twin runs the same fit (sigma schedule and box cull in f32) with
+    # f64 parameters, moments and loss: the two start out equal to rounding
+    # and drift apart only as f32 rounding accumulates.
+    target = np.full((24, 24, 3), 0.4, np.float32)
+    target[6:18, 6:18] = (0.9, 0.2, 0.1)
+    p = np.zeros((6, 10), np.float32)
+    rng = np.random.default_rng(3)
+    p[:, :6] = rng.uniform(0.2, 0.8, (6, 6))
+    p[:, 6:9] = rng.uniform(0, 1, (6, 3))
+    p[:, 9] = 0.5
+    cfg = oracle.FitConfig(iters=40, patience=None)
+    r32 = oracle.fit(target, p, (0.4, 0.4, 0.4), cfg)
+    r64 = oracle.fit(target, p, (0.4, 0.4, 0.4), cfg, f64=True)
+    assert r64.losses.dtype == np.float64 and len(r64.losses) == len(r32.losses) == 40
+    assert abs(r64.losses[0] - r32.losses[0]) <= 1e-6 * r64.losses[0]
+    assert np.all(np.abs(r64.losses - r32.losses) <= 1e-3 * r64.losses)
+    assert r64.best_loss < r64.losses[0]
