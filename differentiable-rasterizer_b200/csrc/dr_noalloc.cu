@@ -15,7 +15,10 @@
 // code must not pass the array's name to a kernel: in host code it is only a
 // stand-in, not a device address. The first call on each device (with that
 // device current) resolves the real address with cudaGetSymbolAddress and
-// caches it; make that first call before any stream capture. Every call
+// caches it; make that first call before any stream capture. Later calls made
+// outside a capture resolve it again (a cheap lookup), so a device reset,
+// which reloads the module and may move the array, never leaves a stale
+// address behind; a call inside a capture uses the cached one. Every call
 // shares the array, so calls whose work overlaps on the GPU (different
 // streams, or different host threads without ordering) race and must be
 // serialized by the caller.
@@ -54,29 +57,38 @@ dr_status noalloc_fail(dr_status s, const char* msg) {
   return s;
 }
 
-// Once per device, with that device current: the device address of the
-// scratch array.
-dr_status scratch_for_current_device(unsigned char** out) {
+// The device address of the scratch array on the current device. Set up on
+// the first call per device (with that device current); refreshed on every
+// call whose stream is not being captured, so the cache never outlives the
+// module it came from. Inside a capture the cached address is used, and a
+// capture before any set-up is an error.
+dr_status scratch_for_current_device(cudaStream_t stream, unsigned char** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return noalloc_fail(DR_NO_DEVICE, "dr_loss_backward_noalloc: no usable current CUDA device");
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    cap = cudaStreamCaptureStatusActive;  // unknown: do not touch the runtime's state
+  }
   unsigned char* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (p) {
+  if (cap != cudaStreamCaptureStatusNone) {
+    if (!p)
+      return noalloc_fail(DR_INVALID_ARGUMENT,
+                          "dr_loss_backward_noalloc: the first call on a device must come "
+                          "before any stream capture");
     *out = p;
     return DR_OK;
   }
   std::lock_guard<std::mutex> lock(g_setup_mu);
-  p = g_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (!p) {
-    void* addr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
-    if (e != cudaSuccess || !addr) {
-      cudaGetLastError();
-      return noalloc_fail(DR_LAUNCH, "dr_loss_backward_noalloc: cudaGetSymbolAddress failed");
-    }
-    p = static_cast<unsigned char*>(addr);
-    g_scratch_ptr[dev].store(p, std::memory_order_release);
+  void* addr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+  if (e != cudaSuccess || !addr) {
+    cudaGetLastError();
+    return noalloc_fail(DR_LAUNCH, "dr_loss_backward_noalloc: cudaGetSymbolAddress failed");
   }
+  p = static_cast<unsigned char*>(addr);
+  g_scratch_ptr[dev].store(p, std::memory_order_release);
   *out = p;
   return DR_OK;
 }
@@ -106,13 +118,13 @@ dr_status dr_loss_backward_noalloc(const float* params, const float* background,
                         "(B*T <= DR_NOALLOC_MAX_TRIANGLES, B <= DR_NOALLOC_MAX_BATCH, "
                         "B*tiles <= DR_NOALLOC_MAX_TILES); use dr_loss_backward");
 
+  cudaStream_t s = (cudaStream_t)stream;
   unsigned char* base = nullptr;
-  dr_status st = scratch_for_current_device(&base);
+  dr_status st = scratch_for_current_device(s, &base);
   if (st) return st;
   TriRec* recs = reinterpret_cast<TriRec*>(base);
   double* partials = reinterpret_cast<double*>(base + kRecBytes);
   unsigned* counters = reinterpret_cast<unsigned*>(base + kRecBytes + kPartialBytes);
-  cudaStream_t s = (cudaStream_t)stream;
 
   // The array keeps the previous call's contents: the tile counters must
   // start at zero, and grads are accumulated into.

@@ -295,9 +295,10 @@ DR_API dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const fl
  * Runs on the current device and `stream`; background is 3 host floats (or
  * NULL for black), shared by the batch; precision is the default. The first
  * call on each device sets up the array's address: make it before any stream
- * capture. All calls share the array, so calls that could overlap on the GPU
- * race: serialize them. Outputs as dr_loss_backward (grads overwritten, losses
- * may be NULL). */
+ * capture. Later calls outside a capture look the address up again, so the
+ * entry point stays valid after a device reset. All calls share the array, so
+ * calls that could overlap on the GPU race: serialize them. Outputs as
+ * dr_loss_backward (grads overwritten, losses may be NULL). */
 #define DR_NOALLOC_MAX_TRIANGLES 16384
 #define DR_NOALLOC_MAX_BATCH 1024
 #define DR_NOALLOC_MAX_TILES 65536
