@@ -1,4 +1,4 @@
-"""``python -m diffrast.kernel_bench``: the path's memory-bound kernels alone.
+"""``python bench_kernels.py``: the path's memory-bound kernels alone.
 
 Prints one JSON line per kernel with its algorithmic bytes, CUDA-event time
 and achieved GB/s against the measured HBM peak. All sizes are far above the
@@ -23,17 +23,23 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import sys
 
-import torch
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "differentiable-rasterizer_b200")
+for _p in (REPO, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
 
-from . import _native
+import torch  # noqa: E402
+
+from diffrast import _native  # noqa: E402
 
 REC_BYTES = 176
 
 
 def _peak_gbs() -> tuple[float, str]:
-    here = os.path.dirname(os.path.abspath(__file__))
-    path = os.path.join(os.path.dirname(os.path.dirname(here)), "MEASURED_PEAKS.json")
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
@@ -98,8 +104,8 @@ def main(argv=None) -> None:
 
 
 def fit_graph(iters: int) -> None:
-    from .fit import mean_color, seed_colors
-    from .scenes import config1_target_scene, seed_scene_geometry
+    from diffrast.fit import mean_color, seed_colors
+    from diffrast.scenes import config1_target_scene, seed_scene_geometry
 
     target = _native.render(torch.from_numpy(config1_target_scene(150, 0)).cuda(), 176, 176,
                             0.0015)[0].contiguous()

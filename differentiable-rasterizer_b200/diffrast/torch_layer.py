@@ -93,20 +93,26 @@ def rasterize(
     channels_first: bool = True,
     device: str = "auto",
 ) -> Tensor:
-    """Render a batch of triangle scenes, differentiably (torch_layer.py:69-108).
+    """Differentiable batched render (same signature as torch_layer.py:69-108).
 
     Args:
-        params: ``(B, T, 10)`` — ``[x0, y0, x1, y1, x2, y2, r, g, b, a]`` per
-            triangle, in normalized image coordinates.
-        height, width: output resolution.
-        sigma: edge softness in normalized units.
-        background: color the canvas is cleared to.
-        channels_first: return ``(B, 3, H, W)`` (written in that layout by the
-            kernel, no permute), else ``(B, H, W, 3)``.
-        device: ``"auto"``, ``"gpu"`` or ``"cuda"`` (all the CUDA kernels).
+        params: ``(B, T, 10)`` float tensor. Each row holds one triangle's three
+            vertices ``x0, y0, x1, y1, x2, y2`` (the unit square maps onto the
+            image), its colour ``r, g, b`` and its opacity ``a``; row 0 is
+            painted first, so later rows cover earlier ones.
+        height, width: image size in pixels.
+        sigma: width of the soft edge, as a fraction of the image side: the
+            coverage of a pixel falls from 1 to 0 over a few ``sigma`` around
+            each edge.
+        background: the RGB value every pixel starts from before any triangle
+            is painted.
+        channels_first: ``(B, 3, H, W)`` when true (the kernel writes that
+            layout directly), ``(B, H, W, 3)`` when false.
+        device: ``"auto"``, ``"gpu"`` or ``"cuda"``; every choice runs the
+            CUDA kernels (there is no CPU path).
 
     Returns:
-        The rendered batch, in linear light, on ``params.device``.
+        The images, linear RGB values, on ``params.device``.
     """
     _check_params(params)
     if height <= 0 or width <= 0:

@@ -34,8 +34,12 @@ def test_stepwise_fitter_matches_the_graph_fit():
     step = f.report()
     assert step.stop_reason == graph.stop_reason
     assert len(step.losses) == len(graph.losses) == 60
-    # Same kernels; gradients are f32 atomic sums, so trajectories agree to rounding.
-    np.testing.assert_allclose(step.losses, graph.losses, rtol=1e-3)
+    # Same kernels; gradients are f32 atomic sums whose order varies run to
+    # run, and a fit amplifies those ulp differences step by step (the f32
+    # oracle and its f64 twin drift apart the same way). The first steps agree
+    # tightly, the rest within half a percent.
+    np.testing.assert_allclose(step.losses[:10], graph.losses[:10], rtol=1e-5)
+    np.testing.assert_allclose(step.losses, graph.losses, rtol=5e-3)
     assert step.best_loss < step.losses[0]
 
 
