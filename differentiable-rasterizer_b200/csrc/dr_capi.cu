@@ -58,6 +58,9 @@ constexpr int kMaxSide = 32768;
 constexpr int kMaxBatch = 65535;
 constexpr long long kMaxTris = 1 << 24;
 constexpr int kTileSide = 16;
+// GpuRasterizer::POLL_TIMEOUT (diffrast-gpu/src/lib.rs:229): the bound on every
+// host wait for device work.
+constexpr double kPollTimeoutS = 60.0;
 
 // Restores the caller's current device on scope exit.
 struct DeviceGuard {
@@ -91,6 +94,7 @@ struct dr_ctx {
   int bg_on_device = 0;
   int precision = 0;
   int split_blocks = 0;  // dr_set_triangle_split: 0 automatic, 1 never, k exactly
+  int reduce_mode = DR_REDUCE_WORKGROUP;  // dr_set_reduce_mode (both values: one reduction)
   uint64_t hits = 0, misses = 0;
   Slot recs, partials, counters, bgbuf, split;
   // fit state
@@ -658,9 +662,209 @@ dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params, const float* b
         "downloading losses");
   }
   // The host buffers stay in use until every stream is done, errors included.
-  for (cudaStream_t q : {ctx->io_comp[0], ctx->io_comp[1], ctx->io_copy})
-    chk(cudaStreamSynchronize(q), "host pipeline");
+  // Each wait is bounded (POLL_TIMEOUT, diffrast-gpu/src/lib.rs:223-229); on a
+  // timeout the copies may still be running, and dr_ctx_destroy waits for them.
+  for (cudaStream_t q : {ctx->io_comp[0], ctx->io_comp[1], ctx->io_copy}) {
+    if (err != cudaSuccess) {
+      chk(cudaStreamSynchronize(q), "host pipeline");
+      continue;
+    }
+    const dr_status ws = dr_stream_wait(q, kPollTimeoutS);
+    if (ws == DR_TIMEOUT) return ws;
+    if (ws != DR_OK) chk(cudaStreamSynchronize(q), "host pipeline");
+  }
   if (err != cudaSuccess) return cuda_fail(err, where);
+  return DR_OK;
+}
+
+dr_status dr_backward(dr_ctx* ctx, const float* params, const float* background, int T, int H,
+                      int W, float sigma, const float* target, int layout, int mode, float* grads,
+                      float* loss, float* image, dr_stream_t stream) {
+  if (mode != DR_BACKWARD_TAPED && mode != DR_BACKWARD_RECOMPUTE)
+    return fail(DR_INVALID_ARGUMENT, "unknown backward mode %d", mode);
+  return backward_common(ctx, kModeLoss, params, background, 0, 1, T, H, W, sigma, target, layout,
+                         0, 1, grads, loss, nullptr, image, (cudaStream_t)stream);
+}
+
+dr_status dr_set_reduce_mode(dr_ctx* ctx, int mode) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (mode != DR_REDUCE_DIRECT && mode != DR_REDUCE_WORKGROUP)
+    return fail(DR_INVALID_ARGUMENT, "unknown reduce mode %d", mode);
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  ctx->reduce_mode = mode;
+  return DR_OK;
+}
+
+dr_status dr_get_reduce_mode(dr_ctx* ctx, int* mode) {
+  if (!ctx || !mode) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  *mode = ctx->reduce_mode;
+  return DR_OK;
+}
+
+dr_status dr_loss_backward_timed(dr_ctx* ctx, const float* params, const float* background,
+                                 int bg_per_scene, int B, int T, int H, int W, float sigma,
+                                 const float* targets, int layout, float* grads, float* losses,
+                                 dr_backward_timings* timings, dr_stream_t stream) {
+  if (!timings) return fail(DR_INVALID_ARGUMENT, "null timings pointer");
+  memset(timings, 0, sizeof(*timings));
+  dr_status st = check_common(ctx, params, B, T, H, W, sigma, layout);
+  if (st) return st;
+  if (B > 0 && (!targets || !losses || (T > 0 && !grads)))
+    return fail(DR_INVALID_ARGUMENT, "null target, losses or grads pointer");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  if (B == 0) return DR_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t np = (size_t)B * T * kParams, nt = (size_t)B * H * W * 3;
+  const int tiles = ((W + kTileSide - 1) / kTileSide) * ((H + kTileSide - 1) / kTileSide);
+  const int k = ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(B, T, tiles);
+  // alloc: the pool grows on the host clock (cudaMalloc is not stream work).
+  const auto a0 = std::chrono::steady_clock::now();
+  if ((st = ensure(ctx, ctx->io_params, sizeof(float) * np, false))) return st;
+  if ((st = ensure(ctx, ctx->io_targets, sizeof(float) * nt, false))) return st;
+  if ((st = ensure(ctx, ctx->io_grads, sizeof(float) * np, false))) return st;
+  if ((st = ensure(ctx, ctx->io_losses, sizeof(float) * (size_t)B, false))) return st;
+  if ((st = ensure(ctx, ctx->recs, tri_rec_bytes() * (size_t)B * T, false))) return st;
+  if ((st = ensure(ctx, ctx->partials, sizeof(double) * (size_t)B * tiles, false))) return st;
+  if ((st = ensure(ctx, ctx->counters, sizeof(unsigned) * (size_t)B, true))) return st;
+  if (k > 1 && (st = ensure(ctx, ctx->split, raster_split_bytes(B, k, H, W), false))) return st;
+  if (background && bg_per_scene &&
+      (st = ensure(ctx, ctx->bgbuf, sizeof(float) * 3 * (size_t)B, false)))
+    return st;
+  timings->alloc_ms =
+      (float)std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - a0)
+          .count();
+  cudaEvent_t ev[4] = {};
+  cudaError_t err = cudaSuccess;
+  const char* where = "";
+  auto chk = [&](cudaError_t e, const char* what) {
+    if (err == cudaSuccess && e != cudaSuccess) {
+      err = e;
+      where = what;
+    }
+  };
+  for (cudaEvent_t& e : ev) chk(cudaEventCreate(&e), "creating timing events");
+  float* P = (float*)ctx->io_params.ptr;
+  float* Tg = (float*)ctx->io_targets.ptr;
+  float* G = (float*)ctx->io_grads.ptr;
+  float* L = (float*)ctx->io_losses.ptr;
+  RasterArgs a;
+  base_args(ctx, B, T, H, W, sigma, layout, a);
+  if (err == cudaSuccess) {
+    chk(cudaEventRecord(ev[0], s), "recording an event");
+    // pack: uploads and the set-up kernel.
+    if (T > 0)
+      chk(cudaMemcpyAsync(P, params, sizeof(float) * np, cudaMemcpyHostToDevice, s),
+          "uploading parameters");
+    chk(cudaMemcpyAsync(Tg, targets, sizeof(float) * nt, cudaMemcpyHostToDevice, s),
+        "uploading targets");
+    if (background && bg_per_scene) {
+      chk(cudaMemcpyAsync(ctx->bgbuf.ptr, background, sizeof(float) * 3 * (size_t)B,
+                          cudaMemcpyHostToDevice, s),
+          "uploading backgrounds");
+      a.bg_dev = (const float*)ctx->bgbuf.ptr;
+      a.bg_per_scene = 1;
+    } else if (background) {
+      a.bg3[0] = background[0];
+      a.bg3[1] = background[1];
+      a.bg3[2] = background[2];
+    }
+    a.recs = (const TriRec*)ctx->recs.ptr;
+    chk(launch_setup(P, B * T, W, H, sigma, 1, (TriRec*)ctx->recs.ptr, s), "set-up kernel");
+    chk(cudaEventRecord(ev[1], s), "recording an event");
+    // dispatch: the fused kernel.
+    if (T > 0) chk(cudaMemsetAsync(G, 0, sizeof(float) * np, s), "zeroing gradients");
+    a.other = Tg;
+    a.grads = G;
+    a.losses = L;
+    a.loss_partials = (double*)ctx->partials.ptr;
+    a.loss_counters = (unsigned*)ctx->counters.ptr;
+    if (k > 1)
+      chk(launch_raster_split(kModeLoss, a, tiles, k, (float4*)ctx->split.ptr, s),
+          "split raster kernels");
+    else
+      chk(launch_raster(kModeLoss, a, tiles, s), "raster kernel");
+    chk(cudaEventRecord(ev[2], s), "recording an event");
+    // readback.
+    if (T > 0)
+      chk(cudaMemcpyAsync(grads, G, sizeof(float) * np, cudaMemcpyDeviceToHost, s),
+          "downloading gradients");
+    chk(cudaMemcpyAsync(losses, L, sizeof(float) * B, cudaMemcpyDeviceToHost, s),
+        "downloading losses");
+    chk(cudaEventRecord(ev[3], s), "recording an event");
+  }
+  dr_status ws = DR_OK;
+  if (err == cudaSuccess) {
+    ws = dr_stream_wait(stream, kPollTimeoutS);
+    if (ws == DR_OK) {
+      chk(cudaEventElapsedTime(&timings->pack_ms, ev[0], ev[1]), "reading timing events");
+      chk(cudaEventElapsedTime(&timings->dispatch_ms, ev[1], ev[2]), "reading timing events");
+      chk(cudaEventElapsedTime(&timings->readback_ms, ev[2], ev[3]), "reading timing events");
+    }
+  } else {
+    cudaStreamSynchronize(s);  // nothing of ours may still read the caller's buffers
+  }
+  for (cudaEvent_t e : ev)
+    if (e) cudaEventDestroy(e);
+  if (ws != DR_OK) return ws;
+  if (err != cudaSuccess) return cuda_fail(err, where);
+  timings->loss_ms = 0.0f;
+  return DR_OK;
+}
+
+uint64_t dr_tape_bytes(uint64_t n_tris, uint64_t width, uint64_t height) {
+  return n_tris * width * height * 3 * 4;
+}
+
+uint64_t dr_scratch_bytes(dr_ctx* ctx, int B, int T, int H, int W) {
+  if (!ctx || B < 0 || T < 0 || H <= 0 || W <= 0) return 0;
+  const int tiles = ((W + kTileSide - 1) / kTileSide) * ((H + kTileSide - 1) / kTileSide);
+  int k = 1;
+  {
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    DeviceGuard g(ctx->device);
+    k = ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(B, T, tiles);
+  }
+  uint64_t b = (uint64_t)tri_rec_bytes() * B * T + sizeof(double) * (uint64_t)B * tiles +
+               sizeof(unsigned) * (uint64_t)B;
+  if (k > 1) b += raster_split_bytes(B, k, H, W);
+  return b;
+}
+
+int dr_is_discrete(int device) {
+  int n = dr_device_count();
+  if (device < 0 || device >= n) return -1;
+  int integrated = 0;
+  if (cudaDeviceGetAttribute(&integrated, cudaDevAttrIntegrated, device) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return integrated ? 0 : 1;
+}
+
+dr_status dr_device_alloc(dr_ctx* ctx, size_t bytes, void** out) {
+  if (!ctx || !out) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  *out = nullptr;
+  DeviceGuard g(ctx->device);
+  DR_CUDA(cudaMalloc(out, bytes ? bytes : 1), "cudaMalloc");
+  return DR_OK;
+}
+
+dr_status dr_device_free(dr_ctx* ctx, void* ptr) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (!ptr) return DR_OK;
+  DeviceGuard g(ctx->device);
+  DR_CUDA(cudaFree(ptr), "cudaFree");
+  return DR_OK;
+}
+
+dr_status dr_memcpy(dr_ctx* ctx, void* dst, const void* src, size_t bytes, dr_stream_t stream) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (bytes == 0) return DR_OK;
+  if (!dst || !src) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  DeviceGuard g(ctx->device);
+  DR_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, (cudaStream_t)stream), "copy");
   return DR_OK;
 }
 

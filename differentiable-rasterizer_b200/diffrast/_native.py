@@ -22,6 +22,8 @@ LIB_PATH = os.path.join(_HERE, "libdiffrast_cuda.so")
 OK, INVALID_ARGUMENT, TOO_LARGE, NO_DEVICE, TIMEOUT, LAUNCH, COMM, OUT_OF_MEMORY, INTERNAL = range(9)
 LAYOUT_BHWC, LAYOUT_BCHW = 0, 1
 PATH_TILE, PATH_REGION, PATH_SPLIT = 0, 1, 2  # dr_path
+BACKWARD_TAPED, BACKWARD_RECOMPUTE = 0, 1  # dr_backward_mode (BackwardMode)
+REDUCE_DIRECT, REDUCE_WORKGROUP = 0, 1  # dr_reduce_mode (ReduceMode)
 STOP_COMPLETED, STOP_CONVERGED, STOP_DIVERGED = 0, 1, 2
 N_PARAMS = 10
 
@@ -55,6 +57,14 @@ class FitReportC(ctypes.Structure):
         ("stop_reason", ctypes.c_int),
         ("config_error", ctypes.c_int),
     ]
+
+
+class BackwardTimingsC(ctypes.Structure):
+    """dr_backward_timings (BackwardTimings, diffrast-gpu/src/lib.rs:96-114)."""
+
+    _fields_ = [("pack_ms", ctypes.c_float), ("alloc_ms", ctypes.c_float),
+                ("dispatch_ms", ctypes.c_float), ("readback_ms", ctypes.c_float),
+                ("loss_ms", ctypes.c_float)]
 
 
 class PoolStatsC(ctypes.Structure):
@@ -98,6 +108,18 @@ SIGNATURES = {
              ctypes.POINTER(FitReportC), _P]),
     "dr_loss_backward_noalloc": (
         _I, [_P, _P, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P]),
+    "dr_backward": (_I, [_P, _P, _P, _I, _I, _I, _F, _P, _I, _I, _P, _P, _P, _P]),
+    "dr_set_reduce_mode": (_I, [_P, _I]),
+    "dr_get_reduce_mode": (_I, [_P, ctypes.POINTER(_I)]),
+    "dr_loss_backward_timed": (
+        _I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P,
+             ctypes.POINTER(BackwardTimingsC), _P]),
+    "dr_tape_bytes": (ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]),
+    "dr_scratch_bytes": (ctypes.c_uint64, [_P, _I, _I, _I, _I]),
+    "dr_is_discrete": (_I, [_I]),
+    "dr_device_alloc": (_I, [_P, ctypes.c_size_t, ctypes.POINTER(_P)]),
+    "dr_device_free": (_I, [_P, _P]),
+    "dr_memcpy": (_I, [_P, _P, _P, ctypes.c_size_t, _P]),
     "dr_pool_stats_get": (_I, [_P, ctypes.POINTER(PoolStatsC)]),
     "dr_clear_pool": (_I, [_P]),
     "dr_stream_wait": (_I, [_P, ctypes.c_double]),
@@ -212,6 +234,41 @@ def query_path(B: int, T: int, height: int, width: int,
     dev = _resolve_device(device)
     out = ctypes.c_int(-1)
     check(lib().dr_query_path(context(dev, _stream(dev)), B, T, height, width, ctypes.byref(out)))
+    return out.value
+
+
+def tape_bytes(n_tris: int, width: int, height: int) -> int:
+    """dr_tape_bytes: what the reference's taped backward would store (this
+    library stores no tape)."""
+    return int(lib().dr_tape_bytes(n_tris, width, height))
+
+
+def scratch_bytes(B: int, T: int, height: int, width: int,
+                  device: torch.device | None = None) -> int:
+    """dr_scratch_bytes: device scratch a loss/gradient call of this shape holds."""
+    dev = _resolve_device(device)
+    return int(lib().dr_scratch_bytes(context(dev, _stream(dev)), B, T, height, width))
+
+
+def is_discrete(index: int = 0) -> bool:
+    """dr_is_discrete (GpuRasterizer::is_discrete)."""
+    v = lib().dr_is_discrete(index)
+    if v < 0:
+        raise DiffrastError(NO_DEVICE, f"no CUDA device {index}")
+    return bool(v)
+
+
+def set_reduce_mode(mode: int, device: torch.device | None = None) -> None:
+    """dr_set_reduce_mode (ReduceMode): accepted for compatibility; both values
+    run the same warp + shared-memory + one-atomic-per-CTA reduction."""
+    dev = _resolve_device(device)
+    check(lib().dr_set_reduce_mode(context(dev, _stream(dev)), int(mode)))
+
+
+def get_reduce_mode(device: torch.device | None = None) -> int:
+    dev = _resolve_device(device)
+    out = ctypes.c_int(-1)
+    check(lib().dr_get_reduce_mode(context(dev, _stream(dev)), ctypes.byref(out)))
     return out.value
 
 
@@ -362,6 +419,58 @@ def loss_backward(params: torch.Tensor, targets: torch.Tensor, sigma: float,
     if want_image:
         return losses, grads, image
     return losses, grads
+
+
+def backward_single(params: torch.Tensor, target: torch.Tensor, sigma: float,
+                    background=(0.0, 0.0, 0.0), mode: int = BACKWARD_RECOMPUTE,
+                    layout: int = LAYOUT_BHWC, want_image: bool = False,
+                    device: torch.device | None = None):
+    """dr_backward: one scene (T, 10) against one target (GpuRasterizer::backward_with).
+    Returns (loss (1,), grads (T, 10)[, image])."""
+    sigma = _check_sigma(sigma)
+    dev = _resolve_device(device if device is not None else params.device)
+    p = _as_cuda_f32(params, dev)
+    t = _as_cuda_f32(target, dev)
+    if p.dim() != 2 or p.shape[1] != N_PARAMS:
+        raise ValueError("params must be (T, 10)")
+    T = p.shape[0]
+    H, W = (t.shape[1], t.shape[2]) if layout == LAYOUT_BCHW else (t.shape[0], t.shape[1])
+    grads = torch.empty((T, N_PARAMS), dtype=torch.float32, device=dev)
+    loss = torch.empty((1,), dtype=torch.float32, device=dev)
+    image = torch.empty_like(t) if want_image else None
+    bg, _ = _bg_host(background, 1)
+    s = _stream(dev)
+    check(lib().dr_backward(context(dev, s), _ptr(p), _ptr(bg), T, H, W, sigma, _ptr(t), layout,
+                            int(mode), _ptr(grads), _ptr(loss), _ptr(image), ctypes.c_void_p(s)))
+    if want_image:
+        return loss, grads, image
+    return loss, grads
+
+
+def loss_backward_timed(params: torch.Tensor, targets: torch.Tensor, sigma: float,
+                        background=(0.0, 0.0, 0.0), layout: int = LAYOUT_BHWC,
+                        device: torch.device | None = None):
+    """dr_loss_backward_timed (backward_many_timed): host tensors in and out,
+    phase by phase. Returns (losses, grads, timings dict in ms)."""
+    sigma = _check_sigma(sigma)
+    dev = _resolve_device(device)
+    p = params.detach().to(torch.float32).contiguous()
+    t = targets.detach().to(torch.float32).contiguous()
+    if p.is_cuda or t.is_cuda:
+        raise ValueError("loss_backward_timed takes host tensors")
+    B, T = p.shape[0], p.shape[1]
+    H, W = (t.shape[2], t.shape[3]) if layout == LAYOUT_BCHW else (t.shape[1], t.shape[2])
+    grads = torch.empty((B, T, N_PARAMS), dtype=torch.float32)
+    losses = torch.empty((B,), dtype=torch.float32)
+    bg, per = _bg_host(background, B)
+    tm = BackwardTimingsC()
+    s = _stream(dev)
+    check(lib().dr_loss_backward_timed(context(dev, s), _ptr(p), _ptr(bg), per, B, T, H, W,
+                                       sigma, _ptr(t), layout, _ptr(grads), _ptr(losses),
+                                       ctypes.byref(tm), ctypes.c_void_p(s)))
+    timings = {f: getattr(tm, f) for f, _ in BackwardTimingsC._fields_}
+    timings["total_ms"] = sum(timings.values())
+    return losses, grads, timings
 
 
 def grad_backward(params: torch.Tensor, grad_images: torch.Tensor, sigma: float,

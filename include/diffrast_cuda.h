@@ -307,6 +307,96 @@ DR_API dr_status dr_loss_backward_noalloc(const float* params, const float* back
                                           int layout, float* grads, float* losses,
                                           dr_stream_t stream);
 
+/* --- the rest of GpuRasterizer's surface ---------------------------------- */
+
+/* BackwardMode (diffrast-gpu/src/lib.rs:211-220): how the reference's
+ * single-scene backward recovers the canvas beneath each triangle, from a
+ * stored tape (Taped) or by re-walking the triangles (Recompute). This
+ * library's backward keeps no tape and needs no O(T^2) re-walk (it takes the
+ * attenuation from two prefix products), so both values run the same kernel and
+ * give the same results; both are accepted so that callers keep working. */
+typedef enum dr_backward_mode { DR_BACKWARD_TAPED = 0, DR_BACKWARD_RECOMPUTE = 1 } dr_backward_mode;
+
+/* One scene's forward + MSE + backward with an explicit mode. Replaces
+ * GpuRasterizer::backward / backward_with (diffrast-gpu/src/lib.rs:503-604).
+ * params (T,10), target (H,W,3) or (3,H,W) per layout, grads (T,10), loss (1
+ * float, may be NULL) and image (may be NULL) are device memory; background as
+ * for dr_loss_backward (3 floats). Same results as dr_loss_backward with B = 1.
+ * Any mode other than the two above is DR_INVALID_ARGUMENT. */
+DR_API dr_status dr_backward(dr_ctx* ctx, const float* params, const float* background, int T,
+                             int H, int W, float sigma, const float* target, int layout, int mode,
+                             float* grads, float* loss, float* image, dr_stream_t stream);
+
+/* ReduceMode (diffrast-gpu/src/lib.rs:76-84): how the batched backward sums
+ * gradients, per contributing pixel (Direct) or per workgroup (Workgroup, the
+ * reference's default). This library always reduces each warp's 32 pixels with
+ * shuffles, each CTA's warps in shared memory, and issues one global atomic per
+ * (triangle, parameter, CTA); both values select that reduction, so results do
+ * not depend on the value. The setting is kept per context (default
+ * DR_REDUCE_WORKGROUP) and read back by dr_get_reduce_mode. */
+typedef enum dr_reduce_mode { DR_REDUCE_DIRECT = 0, DR_REDUCE_WORKGROUP = 1 } dr_reduce_mode;
+DR_API dr_status dr_set_reduce_mode(dr_ctx* ctx, int mode);
+DR_API dr_status dr_get_reduce_mode(dr_ctx* ctx, int* mode);
+
+/* BackwardTimings (diffrast-gpu/src/lib.rs:96-114): where the time of one
+ * host-buffer loss + backward call went, in milliseconds.
+ *   pack_ms      uploads of params, backgrounds and targets, plus the set-up
+ *                kernel that packs the triangle records (CUDA events)
+ *   alloc_ms     growing the context's scratch pool (host clock; 0 when every
+ *                buffer was a pool hit)
+ *   dispatch_ms  the fused forward + MSE + backward kernel (CUDA events)
+ *   readback_ms  downloads of gradients and losses (CUDA events)
+ *   loss_ms      0: the per-image MSE is reduced inside the dispatch, where the
+ *                reference reduced it on the host afterwards
+ * total = the sum of the five. */
+typedef struct dr_backward_timings {
+  float pack_ms, alloc_ms, dispatch_ms, readback_ms, loss_ms;
+} dr_backward_timings;
+
+/* dr_loss_backward on HOST buffers (params (B,T,10), targets, grads (B,T,10),
+ * losses (B,)), run phase by phase on `stream` with events between the phases,
+ * filling *timings. Replaces GpuRasterizer::backward_many_timed
+ * (diffrast-gpu/src/lib.rs:656-663, 676-816). Like the reference's timed form,
+ * the phases do not overlap, so it is slower than dr_loss_backward_host; the
+ * breakdown is a diagnostic. Returns after the results are in host memory, or
+ * DR_TIMEOUT after 60 s (the reference's POLL_TIMEOUT); after a timeout the
+ * host buffers stay in use until the device finishes (dr_ctx_destroy waits). */
+DR_API dr_status dr_loss_backward_timed(dr_ctx* ctx, const float* params,
+                                        const float* background, int bg_per_scene, int B, int T,
+                                        int H, int W, float sigma, const float* targets,
+                                        int layout, float* grads, float* losses,
+                                        dr_backward_timings* timings, dr_stream_t stream);
+
+/* GpuRasterizer::tape_bytes (diffrast-gpu/src/lib.rs:391-393): the bytes the
+ * reference's taped mode stores for T triangles at width x height,
+ * T * width * height * 3 * 4. This library stores no tape (DR_BACKWARD_TAPED
+ * allocates none of it); the device scratch its calls do use is
+ * dr_scratch_bytes. */
+DR_API uint64_t dr_tape_bytes(uint64_t n_tris, uint64_t width, uint64_t height);
+
+/* Device scratch a context holds for a loss or gradient call of B scenes of T
+ * triangles at H x W (triangle records, loss partials and counters, and the
+ * triangle-split state when the call is too small to fill the GPU). No
+ * reference counterpart. Returns 0 for invalid sizes. */
+DR_API uint64_t dr_scratch_bytes(dr_ctx* ctx, int B, int T, int H, int W);
+
+/* GpuRasterizer::is_discrete (diffrast-gpu/src/lib.rs:379-388): 1 for a
+ * discrete GPU, 0 for one integrated with the host, -1 for no such device. */
+DR_API int dr_is_discrete(int device);
+
+/* --- device memory for bindings without a CUDA runtime -------------------- */
+
+/* For callers that bind only this library (the Rust shim, ctypes): device
+ * buffers on the context's device, and copies between any two of host and
+ * device memory (the direction follows from the pointers, unified addressing).
+ * dr_memcpy is ordered on `stream`; a copy into or out of pageable host memory
+ * completes before it returns. No reference counterpart (wgpu owned all
+ * buffers). */
+DR_API dr_status dr_device_alloc(dr_ctx* ctx, size_t bytes, void** out);
+DR_API dr_status dr_device_free(dr_ctx* ctx, void* ptr);
+DR_API dr_status dr_memcpy(dr_ctx* ctx, void* dst, const void* src, size_t bytes,
+                           dr_stream_t stream);
+
 /* --- pool / sync ---------------------------------------------------------- */
 
 /* PoolStats (diffrast-gpu/src/lib.rs:153-158): scratch reuse counters. */

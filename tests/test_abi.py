@@ -107,3 +107,25 @@ def test_host_chunks_cover_the_batch_in_order():
         assert all(ch[i][1] == ch[i + 1][0] for i in range(len(ch) - 1))
         assert len(ch) <= 5
     assert [hi - lo for lo, hi in host_chunks(32)] == [2, 6, 8, 8, 8]
+
+
+def test_reference_surface_without_a_device():
+    # GpuRasterizer::tape_bytes is T * W * H * 3 * 4 (diffrast-gpu/src/lib.rs:391-393);
+    # the other new entry points reject a null context before any CUDA call.
+    from diffrast import _native
+
+    L = _native.lib()
+    assert L.dr_tape_bytes(512, 256, 256) == 512 * 256 * 256 * 3 * 4
+    assert _native.tape_bytes(0, 8, 8) == 0
+    assert L.dr_scratch_bytes(None, 1, 1, 8, 8) == 0
+    assert L.dr_backward(None, None, None, 1, 8, 8, 0.01, None, 0, 0, None, None, None,
+                         None) == _native.INVALID_ARGUMENT
+    assert L.dr_set_reduce_mode(None, 0) == _native.INVALID_ARGUMENT
+    tm = _native.BackwardTimingsC()
+    assert L.dr_loss_backward_timed(None, None, None, 0, 1, 1, 8, 8, 0.01, None, 0, None, None,
+                                    ctypes.byref(tm), None) == _native.INVALID_ARGUMENT
+    assert L.dr_device_alloc(None, 16, ctypes.byref(ctypes.c_void_p())) == \
+        _native.INVALID_ARGUMENT
+    assert L.dr_memcpy(None, None, None, 4, None) == _native.INVALID_ARGUMENT
+    if not has_gpu():
+        assert L.dr_is_discrete(0) == -1
