@@ -129,3 +129,23 @@ def test_reference_surface_without_a_device():
     assert L.dr_memcpy(None, None, None, 4, None) == _native.INVALID_ARGUMENT
     if not has_gpu():
         assert L.dr_is_discrete(0) == -1
+
+
+def _param_counts(text, pattern):
+    out = {}
+    for m in re.finditer(pattern, text, re.S | re.M):
+        args = " ".join(m.group(2).split())
+        out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def test_rust_ffi_block_matches_the_header():
+    # bindings/rust/diffrast-cuda cannot be compiled in this image (no cargo);
+    # its extern block must still declare every C entry point, each with the
+    # header's number of parameters.
+    header = open(os.path.join(HEADER_DIR, "diffrast_cuda.h")).read()
+    ffi = open(os.path.join(REPO, "bindings", "rust", "diffrast-cuda", "src", "ffi.rs")).read()
+    c = _param_counts(header, r"^DR_API\s+[\w\s\*]+?\b(dr_\w+)\s*\(([^)]*)\)")
+    rs = _param_counts(ffi, r"pub fn (dr_\w+)\(([^)]*)\)")
+    assert set(c) == declared_symbols()
+    assert c == rs
