@@ -11,8 +11,19 @@ metric counts dense pairs B*T*H*W per step, as the reference's own
 Timing: W untimed warm-up steps; then K steps, each preceded by an untimed L2
 flush (a 256 MiB write; the working set is smaller than the 126 MB L2), each
 timed with CUDA events on the launching stream; barrier + synchronize around
-the timed region; the MAX over ranks. Multi-GPU (torchrun): every rank runs its
-own batch of 32 scenes (weak scaling, no data-path collective).
+the timed region; the MAX over ranks. Multi-GPU (torchrun): the 32-scene batch
+is split over the ranks, 32/N scenes each (strong scaling, as benchmark config 2
+is stated; no data-path collective); `--scaling weak` gives every rank its own
+32. Under torchrun the line also carries config 4 row-sharded over the ranks
+(`config4_sharded`: the in-place NCCL all-reduce of the gradient inside the
+step).
+
+At N=1 the line carries secondary measurements: the config 1 fit (`secondary`),
+every other benchmark config timed on this GPU with its oracle CPU rate on a
+bounded sample (`configs`: the config 2 grid at sigma 0.0015 and 0.01, the
+config 3 torch op with its e2e, config 4, config 5 at three sigmas), the box's
+CPU model and core count (`host`), and the oracle's single-thread calibration
+against the reference's published i9 times (`cpu_baseline.calibration`).
 
 `e2e` is the same metric through the public torch API with host (pinned)
 buffers: diffrast.torch_layer.fused_loss on CPU tensors, so every step copies
@@ -59,6 +70,11 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fit", action="store_true", help="skip the secondary fit metric")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-config secondary lines (configs 2-5)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="N>1: split the 32-scene batch over the ranks (strong, config 2 as "
+                         "BASELINE.json states it) or give every rank its own 32 (weak)")
     return ap.parse_args()
 
 
@@ -79,6 +95,13 @@ def inputs(rank: int):
     params = uniform_scenes(B, T, 2000 + CELL + 1000 * rank)
     target_scenes = uniform_scenes(B, T, 3000 + CELL + 1000 * rank)
     return params, target_scenes
+
+
+def rank_slice(rank: int, world: int) -> tuple[int, int]:
+    """Scenes [lo, hi) of the 32-scene batch that rank `rank` of `world` owns
+    under strong scaling: contiguous, as even as possible."""
+    lo = rank * B // world
+    return lo, (rank + 1) * B // world
 
 
 class ClockSampler:
@@ -212,6 +235,245 @@ def fit_metric(dev, with_cpu: bool):
     return out
 
 
+def host_identity() -> dict:
+    """CPU model and logical core count of the box the CPU baselines run on."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count()}
+
+
+SFU_PER_PAIR = 7  # fwd 3 + bwd 4 MUFU operations per bounding-box pair
+
+
+def peaks_at(sm_mhz: float, sms: int):
+    """Nominal FP32 FLOP/s and SFU op/s at a clock: 148 SMs x 128 FP32 lanes x 2
+    and 148 SMs x 16 SFU lanes on a B200."""
+    return sms * 128 * 2 * sm_mhz * 1e6, sms * 16 * sm_mhz * 1e6
+
+
+def time_device(fn, steps: int, warmup: int, flush, stream) -> float:
+    """Median CUDA-event time of fn() in ms, L2 flushed before every call."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(steps):
+        flush.fill_(1)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        ev.append((e0, e1))
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in ev)
+
+
+def cpu_sample_rate(params, target, sigma, threads: int, budget_s: float):
+    """The oracle's fwd+loss+bwd on a bounded sample: the first n scenes, n
+    chosen from one timed scene so that the sample takes about budget_s.
+    Returns (dense pairs/s, seconds, scenes)."""
+    import oracle
+
+    B, T = params.shape[:2]
+    H, W = target.shape[1], target.shape[2]
+    t0 = time.perf_counter()
+    oracle.backward_batch(params[:1], target[:1], sigma, threads=1)
+    one = max(time.perf_counter() - t0, 1e-6)
+    n = int(max(1, min(B, budget_s * min(threads, B) / one)))
+    t0 = time.perf_counter()
+    oracle.backward_batch(params[:n], target[:n], sigma, threads=threads)
+    dt = time.perf_counter() - t0
+    return n * T * H * W / dt, dt, n
+
+
+def config_line(name, workload, ms, dense, bbox, sm_mhz, sms, cpu=None, **extra):
+    fp32, sfu = peaks_at(sm_mhz, sms)
+    s = ms / 1e3
+    line = {"config": name, "workload": workload, "ms_per_step": ms,
+            "dense_pair_evals_per_s": dense / s, "bbox_pair_evals_per_s": bbox / s,
+            "bbox_pairs": bbox,
+            "fp32_frac": bbox * FLOP_PER_PAIR / s / fp32,
+            "sfu_frac": bbox * SFU_PER_PAIR / s / sfu}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    line.update(extra)
+    return line
+
+
+def run_configs(dev, sm_mhz: float, with_cpu: bool, budget_s: float = 1.5):
+    """Secondary timed lines for every benchmark configuration (BASELINE.json
+    configs 2-5) on this GPU, each with its oracle CPU rate on a bounded sample
+    when with_cpu. Device-resident inputs, L2 flushed before every step."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+
+    import oracle
+    from diffrast import _native, torch_layer
+    from diffrast import scenes as S
+
+    if with_cpu:
+        oracle.build()
+    thr = oracle.num_threads() if with_cpu else 0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    out = []
+
+    def cpu_dict(rate, dt, n, total, threads):
+        return {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"{n} of {total} scenes, {dt:.2f} s"}
+
+    # Config 2: the 9-cell grid at sigma 0.0015 and 0.01 (B=32).
+    for sigma in (0.0015, 0.01):
+        for ti, tris in enumerate((32, 128, 512)):
+            for si, size in enumerate((64, 128, 256)):
+                p, tp = S.config2_params(32, tris, ti * 3 + si)
+                P = torch.from_numpy(p).to(dev)
+                tgt = _native.render(torch.from_numpy(tp).to(dev), size, size, sigma)
+                ms = time_device(lambda: _native.loss_backward(P, tgt, sigma), 20, 3, flush,
+                                 stream)
+                cpu = None
+                if with_cpu:
+                    rate, dt, n = cpu_sample_rate(p, tgt.cpu().numpy(), sigma, thr, budget_s / 3)
+                    cpu = cpu_dict(rate, dt, n, 32, thr)
+                out.append(config_line(
+                    "config2", f"B=32 T={tris} {size}x{size} sigma={sigma} fwd+mse+bwd", ms,
+                    32 * tris * size * size, S.bbox_pairs(p, size, size, sigma), sm_mhz, sms, cpu,
+                    path=_native.query_path(32, tris, size, size)))
+
+    # Config 3: the torch op, rasterize -> F.mse_loss -> backward at B=256.
+    g = torch.Generator().manual_seed(2)
+    raw = torch.randn(256, 64, 10, generator=g)
+    params = torch_layer.activate(raw)
+    tparams = torch_layer.random_params(256, 64, generator=torch.Generator().manual_seed(3))
+    targets = torch_layer.rasterize(tparams.to(dev), 128, 128, 0.0015).detach()
+    p_dev = params.to(dev)
+
+    def op_step(p_src):
+        q = p_src.detach().to(dev).requires_grad_(True)
+        loss = F.mse_loss(torch_layer.rasterize(q, 128, 128, 0.0015), targets)
+        loss.backward()
+        return loss, q.grad
+
+    ms = time_device(lambda: op_step(p_dev), 10, 3, flush, stream)
+    p_pin = params.clone().pin_memory()
+    t_pin = targets.cpu().pin_memory()
+
+    def op_step_e2e():
+        q = p_pin.to(dev, non_blocking=True).requires_grad_(True)
+        tg = t_pin.to(dev, non_blocking=True)
+        loss = F.mse_loss(torch_layer.rasterize(q, 128, 128, 0.0015), tg)
+        loss.backward()
+        return loss.item(), q.grad.cpu()
+
+    for _ in range(3):
+        op_step_e2e()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(10):
+        op_step_e2e()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / 10
+    p_np = params.numpy()
+    cpu = None
+    if with_cpu:
+        rate, dt, n = cpu_sample_rate(p_np, targets.permute(0, 2, 3, 1).cpu().numpy(), 0.0015,
+                                      thr, budget_s)
+        cpu = cpu_dict(rate, dt, n, 256, thr)
+    dense = 256 * 64 * 128 * 128
+    out.append(config_line(
+        "config3", "B=256 T=64 128x128 sigma=0.0015 rasterize -> F.mse_loss -> backward "
+                   "(torch op, device tensors)", ms, dense,
+        S.bbox_pairs(p_np, 128, 128, 0.0015), sm_mhz, sms, cpu,
+        e2e={"value": dense / (e2e_ms / 1e3), "unit": UNIT, "ms_per_step": e2e_ms,
+             "h2d_bytes_per_step": p_pin.numel() * 4 + t_pin.numel() * 4,
+             "d2h_bytes_per_step": p_pin.numel() * 4 + 4,
+             "api": "pinned host params and targets copied in, loss and params.grad read "
+                    "back, every step"}))
+
+    # Config 4: one 1024^2 scene, T=4096: fwd+bwd+Adam (one GPU).
+    p4 = S.config4_params(4096, 4000)
+    t4 = _native.render(torch.from_numpy(S.config4_params(4096, 4001)).to(dev), 1024, 1024,
+                        0.0015)
+    P4 = torch.from_numpy(p4).to(dev)
+    m4, v4 = torch.zeros_like(P4), torch.zeros_like(P4)
+    it = [0]
+
+    def step4():
+        losses, grads = _native.loss_backward(P4, t4, 0.0015)
+        it[0] += 1
+        _native.adam_step(P4, m4, v4, grads, it[0])
+
+    ms = time_device(step4, 10, 3, flush, stream)
+    cpu = None
+    if with_cpu:
+        t0 = time.perf_counter()
+        oracle.backward_batch(p4, t4.cpu().numpy(), 0.0015, threads=1)
+        dt = time.perf_counter() - t0
+        cpu = {"value": 4096 * 1024 * 1024 / dt, "unit": UNIT, "cores": 1, "kind": "port",
+               "sample": f"one full step, single thread (a single scene is sequential in the "
+                         f"reference), {dt:.2f} s"}
+    out.append(config_line("config4", "B=1 T=4096 1024x1024 sigma=0.0015 fwd+mse+bwd+Adam",
+                           ms, 4096 * 1024 * 1024, S.bbox_pairs(p4, 1024, 1024, 0.0015), sm_mhz,
+                           sms, cpu, path=_native.query_path(1, 4096, 1024, 1024)))
+
+    # Config 5: B=16, T=2048, 512^2 stress at the three sigmas.
+    p5 = S.config5_params(16, 2048, 5000)
+    P5 = torch.from_numpy(p5).to(dev)
+    for sigma in (0.00015, 0.0015, 0.015):
+        t5 = _native.render(torch.from_numpy(S.config5_params(16, 2048, 5100)).to(dev), 512,
+                            512, sigma)
+        ms = time_device(lambda: _native.loss_backward(P5, t5, sigma), 10, 3, flush, stream)
+        cpu = None
+        if with_cpu:
+            rate, dt, n = cpu_sample_rate(p5, t5.cpu().numpy(), sigma, thr, budget_s)
+            cpu = cpu_dict(rate, dt, n, 16, thr)
+        out.append(config_line("config5", f"B=16 T=2048 512x512 sigma={sigma} fwd+mse+bwd", ms,
+                               16 * 2048 * 512 * 512, S.bbox_pairs(p5, 512, 512, sigma), sm_mhz,
+                               sms, cpu, path=_native.query_path(16, 2048, 512, 512)))
+    return out
+
+
+def calibration(threads: int = 1):
+    """The oracle's single-thread fwd+bwd on the reference's own bench shapes
+    (Scene::random(n, bg, 0.15) small triangles, sigma 0.01) beside the
+    published i9-13900 single-thread times (docs/gpu-report.txt:143,146)."""
+    import numpy as np
+
+    import oracle
+
+    rows = []
+    for size, tris, ref_ms in ((128, 64, 3.02), (256, 256, 48.25)):
+        rng = np.random.default_rng(42)
+        c = rng.uniform(0, 1, size=(1, tris, 1, 2))
+        v = c + rng.uniform(-0.15, 0.15, size=(1, tris, 3, 2))
+        p = np.concatenate([v.reshape(1, tris, 6), rng.uniform(0, 1, (1, tris, 3)),
+                            rng.uniform(0.3, 0.8, (1, tris, 1))], -1).astype(np.float32)
+        tgt = np.full((1, size, size, 3), 0.5, np.float32)
+        oracle.backward_batch(p, tgt, 0.01, threads=threads)
+        reps, t0 = 0, time.perf_counter()
+        while reps < 3 or time.perf_counter() - t0 < 1.0:
+            oracle.backward_batch(p, tgt, 0.01, threads=threads)
+            reps += 1
+        ms = 1e3 * (time.perf_counter() - t0) / reps
+        rows.append({"shape": f"{size}x{size}, {tris} triangles, sigma 0.01", "oracle_ms": ms,
+                     "reference_i9_ms": ref_ms, "ratio": ms / ref_ms})
+    return rows
+
+
 def run_reference(args, rank: int, world: int):
     """--impl reference: the reference CPU algorithm, all host threads."""
     if rank != 0:
@@ -271,6 +533,12 @@ def main():
         import torch.distributed as dist
 
         if args.impl == "ours":
+            # NCCL's communicator set-up lines (ranks, devices, channels) on
+            # stderr, so a log shows how many ranks took part; stdout keeps the
+            # one JSON line.
+            os.environ.setdefault("NCCL_DEBUG", "INFO")
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
             torch.cuda.set_device(local)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", local))
@@ -288,7 +556,13 @@ def main():
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    params_np, tscenes_np = inputs(rank)
+    strong = world > 1 and args.scaling == "strong"
+    if strong:
+        lo, hi = rank_slice(rank, world)
+        params_np, tscenes_np = (a[lo:hi] for a in inputs(0))
+    else:
+        params_np, tscenes_np = inputs(rank)
+    n_local = params_np.shape[0]
     P = torch.from_numpy(params_np).to(dev)
     TS = torch.from_numpy(tscenes_np).to(dev)
     target = _native.render(TS, H, W, SIGMA)  # targets = independent scenes rendered
@@ -328,8 +602,40 @@ def main():
         dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
     total_ms = float(t_ms.item())
     ms_per_step = total_ms / args.steps
-    value = world * dense_pairs(B) / (ms_per_step / 1e3)
+    global_scenes = B if strong else world * B
+    value = dense_pairs(global_scenes) / (ms_per_step / 1e3)
     del grads_dummy
+
+    # Config 4 row-sharded over the ranks: fwd+bwd, the in-place all-reduce of
+    # the 4096 x 10 gradient and the loss sums, and Adam, every step.
+    sharded4 = None
+    if world > 1:
+        from diffrast.scenes import config4_params
+        from diffrast.sharded import ShardedSceneStep
+
+        st4 = ShardedSceneStep(torch.from_numpy(config4_params(4096, 4000)).to(dev))
+        t4 = _native.render(torch.from_numpy(config4_params(4096, 4001)).to(dev), 1024, 1024,
+                            SIGMA)
+        for _ in range(3):
+            st4.step(t4, SIGMA)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(10):
+            st4.step(t4, SIGMA)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms4 = torch.tensor([e0.elapsed_time(e1) / 10], dtype=torch.float64, device=dev)
+        dist.all_reduce(ms4, op=dist.ReduceOp.MAX)
+        sharded4 = {"config": "config4", "workload": f"B=1 T=4096 1024x1024 sigma={SIGMA} "
+                    f"fwd+mse+bwd+all-reduce+Adam, tile rows sharded over {world} GPUs",
+                    "ms_per_step": float(ms4.item()),
+                    "dense_pair_evals_per_s": 4096 * 1024 * 1024 / (float(ms4.item()) / 1e3),
+                    "collective": "NCCL all_reduce of the 4096x10 f32 gradient and the f64 "
+                                  "loss sum, in place"}
+        del st4, t4
 
     # e2e: public API with pinned host buffers (H2D of inputs, D2H of results).
     p_host = torch.from_numpy(params_np).pin_memory()
@@ -354,44 +660,73 @@ def main():
     e2e_ms = float(e2e_ms.item())
     h2d = p_host.numel() * 4 + t_host.numel() * 4
     d2h = losses_h.numel() * 4 + grads_h.numel() * 4
+    # The box's plain pinned upload rate for the same bytes: e2e's copy bound.
+    dst = torch.empty(h2d // 4, dtype=torch.float32, device=dev)
+    src = torch.empty(h2d // 4, dtype=torch.float32).pin_memory()
+    for _ in range(3):
+        dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(10):
+        dst.copy_(src, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    h2d_gbs = h2d / (e0.elapsed_time(e1) / 10 / 1e3) / 1e9
+    del dst, src
 
     if rank == 0:
         pk = peaks()
-        n_bbox = bbox_pairs(params_np)
+        n_bbox = bbox_pairs(params_np)  # this GPU's share of the batch
         sm_mhz = (clock_info or {}).get("sm_mhz") or pk.get("sm_max_mhz", 1965.0)
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        fp32_peak = sms * 128 * 2 * sm_mhz * 1e6 / 1e12  # TFLOP/s at the sampled clock
-        achieved = n_bbox * FLOP_PER_PAIR / (ms_per_step / 1e3) / 1e12
+        fp32_peak, sfu_peak = peaks_at(sm_mhz, sms)
+        achieved = n_bbox * FLOP_PER_PAIR / (ms_per_step / 1e3)
+        sfu_achieved = n_bbox * SFU_PER_PAIR / (ms_per_step / 1e3)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if strong or world == 1 else "weak",
+            "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded PCG64 scenes, config 2 distribution)",
             "config": {"workload": "config2 B=32 T=128 256x256 sigma=0.0015 fwd+mse+bwd "
                                    "(dr_loss_backward)",
-                       "global_batch": B * world, "seq_len": None,
-                       "parallelism": f"batch-sharded x{world} (no collective)",
+                       "global_batch": global_scenes, "seq_len": None,
+                       "parallelism": (f"batch-sharded x{world}: {n_local} scenes per GPU, "
+                                       "no collective"),
                        "l2": "flushed (256 MiB write) before every timed step"},
-            "e2e": {"value": world * dense_pairs(B) / (e2e_ms / 1e3), "unit": UNIT,
+            "e2e": {"value": dense_pairs(global_scenes) / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "pinned_h2d_gbs": h2d_gbs,
+                    "copy_bound_ms": h2d / (h2d_gbs * 1e9) * 1e3,
                     "api": "diffrast.torch_layer.fused_loss on pinned CPU tensors "
                            "(dr_loss_backward_host: chunked upload, kernels and download "
                            "in one call)"},
             "gpu_launches": 2 * args.steps,
-            "roofline": {"bound": "fp32", "achieved": achieved, "peak": fp32_peak,
-                         "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+            "roofline": {"bound": "fp32", "achieved": achieved / 1e12,
+                         "peak": fp32_peak / 1e12, "unit": "TFLOP/s",
+                         "frac": achieved / fp32_peak,
+                         "sfu_achieved": sfu_achieved / 1e12, "sfu_peak": sfu_peak / 1e12,
+                         "sfu_unit": "Tops/s", "sfu_frac": sfu_achieved / sfu_peak,
                          # dram read + write of one raster launch, ncu capture in
                          # profiles/raster_kernel_config2_b32_t128_256.md
                          "traffic": TRAFFIC_BYTES,
                          "pairs_per_step": n_bbox, "flop_per_pair": FLOP_PER_PAIR,
-                         "peak_source": f"nominal FP32 ({sms} SMs x 128 lanes x 2) at the "
-                                        f"sampled SM clock {sm_mhz:.0f} MHz",
+                         "sfu_per_pair": SFU_PER_PAIR,
+                         "peak_source": f"nominal FP32 ({sms} SMs x 128 lanes x 2) and SFU "
+                                        f"({sms} SMs x 16) at the sampled SM clock "
+                                        f"{sm_mhz:.0f} MHz; MEASURED_PEAKS.json has no FP32 "
+                                        "or SFU figure",
                          "timed": "whole step (set-up + raster kernels) per CUDA events"},
             "clocks": clock_info,
+            "host": host_identity(),
         }
-        if not args.no_fit:
+        if sharded4 is not None:
+            line["config4_sharded"] = sharded4
+        if not args.no_fit and world == 1:
             line["secondary"] = fit_metric(dev, not args.no_cpu_baseline)
-        if not args.no_cpu_baseline:
+        if not args.no_configs and world == 1:
+            line["configs"] = run_configs(dev, sm_mhz, not args.no_cpu_baseline)
+        if not args.no_cpu_baseline and world == 1:
             import oracle
 
             tgt_np = target.cpu().numpy()
@@ -401,7 +736,8 @@ def main():
             line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": thr, "kind": "port",
                                     "sample": f"{nsteps} full steps of {ns} scenes ({dt:.1f} s "
                                               f"wall on {thr} threads), C++ restatement of the "
-                                              "Rust CPU path"}
+                                              "Rust CPU path",
+                                    "calibration": calibration()}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

@@ -495,16 +495,27 @@ def grad_backward(params: torch.Tensor, grad_images: torch.Tensor, sigma: float,
 
 
 def loss_backward_sharded(params: torch.Tensor, targets: torch.Tensor, sigma: float, shard: int,
-                          n_shards: int, background=(0.0, 0.0, 0.0), layout: int = LAYOUT_BHWC):
-    """dr_loss_backward_sharded. Returns (loss_sums (B,) f64, partial grads)."""
+                          n_shards: int, background=(0.0, 0.0, 0.0), layout: int = LAYOUT_BHWC,
+                          out=None):
+    """dr_loss_backward_sharded. Returns (loss_sums (B,) f64, partial grads).
+
+    ``out=(grads, sums)`` writes into caller-owned device tensors ((B, T, 10)
+    f32 and (B,) f64, contiguous) instead of new ones."""
     sigma = _check_sigma(sigma)
     dev = _resolve_device(params.device)
     p = _as_cuda_f32(params, dev)
     t = _as_cuda_f32(targets, dev)
     B, T = p.shape[0], p.shape[1]
     H, W = (t.shape[2], t.shape[3]) if layout == LAYOUT_BCHW else (t.shape[1], t.shape[2])
-    grads = torch.empty((B, T, N_PARAMS), dtype=torch.float32, device=dev)
-    sums = torch.empty((B,), dtype=torch.float64, device=dev)
+    if out is None:
+        grads = torch.empty((B, T, N_PARAMS), dtype=torch.float32, device=dev)
+        sums = torch.empty((B,), dtype=torch.float64, device=dev)
+    else:
+        grads, sums = out
+        if (grads.shape != (B, T, N_PARAMS) or grads.dtype != torch.float32
+                or not grads.is_contiguous() or sums.shape != (B,)
+                or sums.dtype != torch.float64 or not grads.is_cuda or not sums.is_cuda):
+            raise ValueError("out must be ((B, T, 10) f32, (B,) f64) contiguous device tensors")
     bg, per = _bg_host(background, B)
     s = _stream(dev)
     check(lib().dr_loss_backward_sharded(context(dev, s), _ptr(p), _ptr(bg), per, B, T, H, W,

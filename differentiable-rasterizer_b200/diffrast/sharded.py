@@ -31,18 +31,6 @@ def shard_rows(height: int, shard: int, n_shards: int) -> list[int]:
     return list(range(shard, tiles_y, n_shards))
 
 
-def pack_for_reduce(grads: torch.Tensor, loss_sums: torch.Tensor) -> torch.Tensor:
-    """One f64 buffer [grads..., loss sums...] so a single collective carries both
-    (summing the partial gradients in f64 also removes the f32 order noise)."""
-    return torch.cat([grads.reshape(-1).to(torch.float64), loss_sums.reshape(-1)])
-
-
-def unpack_reduced(buf: torch.Tensor, grads_shape, batch: int):
-    n = buf.numel() - batch
-    grads = buf[:n].to(torch.float32).reshape(grads_shape)
-    return grads, buf[n:]
-
-
 class ShardedSceneStep:
     """Forward + MSE + backward of one (or a few) large scenes across ranks, then
     Adam with the fit's per-parameter rates and projection (fit.rs:388-424)."""
@@ -62,24 +50,30 @@ class ShardedSceneStep:
         self.v = torch.zeros_like(self.params)
         self.t = 0
         self.lrs = (lr_pos, lr_color, lr_alpha)
+        # The kernel writes this rank's partial gradient and f64 loss sums
+        # straight into these buffers, which the all-reduces then sum in place:
+        # no copies or conversions between the kernel and Adam.
+        self.grads = torch.empty_like(self.params)
+        self.sums = torch.empty(self.params.shape[0], dtype=torch.float64,
+                                device=self.params.device)
 
     def loss_and_grads(self, targets: torch.Tensor, sigma: float, background=(0.0, 0.0, 0.0)):
-        """All-reduced (losses (B,), grads (B, T, 10)) for the current params."""
-        sums, grads = _native.loss_backward_sharded(self.params, targets, sigma, self.rank,
-                                                    self.world, background)
-        buf = pack_for_reduce(grads, sums)
+        """All-reduced (losses (B,), grads (B, T, 10)) for the current params.
+        The returned gradient is the step's buffer: the next call overwrites it."""
+        _native.loss_backward_sharded(self.params, targets, sigma, self.rank, self.world,
+                                      background, out=(self.grads, self.sums))
         if self.world > 1:
-            self.dist.all_reduce(buf, op=self.dist.ReduceOp.SUM, group=self.group)
-        grads, sums = unpack_reduced(buf, grads.shape, self.params.shape[0])
+            self.dist.all_reduce(self.grads, op=self.dist.ReduceOp.SUM, group=self.group)
+            self.dist.all_reduce(self.sums, op=self.dist.ReduceOp.SUM, group=self.group)
         h, w = targets.shape[1], targets.shape[2]
-        losses = (sums / float(h * w * 3)).to(torch.float32)  # canvas.rs:58
-        return losses, grads
+        losses = (self.sums / float(h * w * 3)).to(torch.float32)  # canvas.rs:58
+        return losses, self.grads
 
     def step(self, targets: torch.Tensor, sigma: float, background=(0.0, 0.0, 0.0)):
         """One fit iteration: loss, gradients, Adam + projection. Returns losses."""
         losses, grads = self.loss_and_grads(targets, sigma, background)
         self.t += 1
-        _native.adam_step(self.params, self.m, self.v, grads.contiguous(), self.t, *self.lrs)
+        _native.adam_step(self.params, self.m, self.v, grads, self.t, *self.lrs)
         return losses
 
 
