@@ -21,6 +21,7 @@ SOURCES = [os.path.join(CSRC, f) for f in ("dr_kernels.cu", "dr_capi.cu", "dr_no
 HEADERS = [
     os.path.join(CSRC, "dr_device.cuh"),
     os.path.join(CSRC, "dr_internal.h"),
+    os.path.join(CSRC, "dr_math.cuh"),
     os.path.join(REPO, "include", "diffrast_cuda.h"),
 ]
 LIB = os.path.join(HERE, "diffrast", "libdiffrast_cuda.so")

@@ -25,6 +25,7 @@
 #include <cstdio>
 
 #include "dr_device.cuh"
+#include "dr_math.cuh"
 #include "dr_internal.h"
 
 namespace dr {
@@ -221,6 +222,7 @@ struct Smem {
   unsigned char bcode[kChunk][kBlocksPerTile];
   int kidx[kChunk];
   float acc[kChunk][kParams];
+  float4 stage[kWarps][24];  // one warp block's 96 image values (store_block)
   int warp_count[kWarps];
   double loss_part[kWarps];
   int is_last;
@@ -235,6 +237,7 @@ struct RegionSmem {
   unsigned char bcode[kChunk][kRB];
   int kidx[kChunk];
   float acc[kChunk][kParams];
+  float4 stage[kWarps][24];  // one warp block's 96 image values (store_block)
   int warp_count[kWarps];
   double loss_part[kRB];
   int next_block;
@@ -419,57 +422,6 @@ struct PairEval {
   float dax, day, dbx, dby;
   int edge;
 };
-
-// Quotients and square roots rounded to nearest without the library's
-// special-case branches: the hardware approximation (rcp.approx / rsqrt.approx,
-// relative error below 2^-22) refined by one Newton-Raphson step with an FMA
-// residual (Markstein's method). The refined value is within ~2^-44 of the
-// exact result, so it rounds correctly except for inputs whose exact result
-// lies that close to a rounding midpoint. Valid for normal, positive inputs.
-__device__ __forceinline__ float rcp_approx(float y) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
-  return r;
-}
-__device__ __forceinline__ float rsqrt_approx(float x) {
-  float r;
-  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-// sqrt(x) for x >= 0; inputs below 1e-30 (distances far under the 1e-9 cut
-// of grad.rs:252) return 0.
-__device__ __forceinline__ float sqrt_nr(float x) {
-  const float rs = rsqrt_approx(x);
-  const float s = __fmul_rn(x, rs);
-  const float res = __fmaf_rn(-s, s, x);
-  const float out = __fmaf_rn(res, __fmul_rn(0.5f, rs), s);
-  return x > 1e-30f ? out : 0.0f;
-}
-
-// a / b rounded to nearest, given inv_b within 2^-22 of 1 / b (rcp_approx, or
-// a precomputed RN(1 / b)): one correction step on the product with an FMA
-// residual. For a = 1 this is the Newton-refined reciprocal.
-__device__ __forceinline__ float div_rn_inv(float a, float b, float inv_b) {
-  const float q0 = __fmul_rn(a, inv_b);
-  const float r = __fmaf_rn(-q0, b, a);
-  return __fmaf_rn(r, inv_b, q0);
-}
-
-// Sigmoid of raster.rs:79-87 with its rounding: RN(1 / RN(1 + e)) for x >= 0,
-// RN(e / RN(1 + e)) below, e = exp(-|x|). The exponential may be approximate:
-// its error moves 1 + e by far less than an ulp of 1 wherever e is small,
-// while near cov == 1 the gradient uses 1 - cov, which depends on exactly how
-// the reference rounded cov.
-__device__ __forceinline__ float sigmoid_rounded(float x) {
-  const float e = __expf(-fabsf(x));
-  const float y = __fadd_rn(1.0f, e);
-  return div_rn_inv(x >= 0.0f ? 1.0f : e, y, rcp_approx(y));
-}
-
-__device__ __forceinline__ float sigmoid_fast(float x) {
-  const float e = __expf(-fabsf(x));
-  return __fdividef(x >= 0.0f ? 1.0f : e, __fadd_rn(1.0f, e));
-}
 
 // d(cov)/d(vertices) for the nearest edge with the reference's rounding:
 // cp = a + t (b - a); u = (pt - cp) / dist; chain = cov (1 - cov) / sigma * sign;
@@ -1115,6 +1067,49 @@ __device__ __forceinline__ void store_pixel(const RasterArgs& a, int b, int px, 
   a.image[pix_index(a.layout, b, 2, px, py, a.W, a.H)] = c2;
 }
 
+// One warp block's image (8 x 4 pixels, a pixel per lane, 3 channels) in
+// 16-byte stores: the 96 values go through the warp's shared-memory stage and
+// leave as 24 float4 stores, whole 16-byte runs of the image in either layout
+// (BHWC: 4 rows of 24 consecutive floats; BCHW: 3 channel planes x 4 rows of
+// 8 floats), where scalar stores would write each sector in three passes.
+// Needs every lane of the warp (it synchronizes the warp); blocks that cross
+// the image border, widths that are not a multiple of 4, or an image pointer
+// that is not 16-byte aligned take per-lane scalar stores.
+__device__ __forceinline__ void store_block(const RasterArgs& a, int b, int x0, int y0, int lane,
+                                            float c0, float c1, float c2, float4* stage) {
+  const int px = x0 + (lane & 7), py = y0 + (lane >> 3);
+  const bool whole = x0 + kBlockW <= a.W && y0 + kBlockH <= a.H && (a.W & 3) == 0 &&
+                     ((uintptr_t)a.image & 15u) == 0;
+  if (!whole) {
+    if (px < a.W && py < a.H) store_pixel(a, b, px, py, c0, c1, c2);
+    return;
+  }
+  float* st = reinterpret_cast<float*>(stage);
+  __syncwarp();  // the previous block's reads of the stage are done
+  if (a.layout == kLayoutBCHW) {
+    st[lane] = c0;
+    st[32 + lane] = c1;
+    st[64 + lane] = c2;
+  } else {
+    st[3 * lane] = c0;  // stride 3 words: 32 distinct banks
+    st[3 * lane + 1] = c1;
+    st[3 * lane + 2] = c2;
+  }
+  __syncwarp();
+  if (lane < 24) {
+    const float4 v = stage[lane];
+    float* dst;
+    if (a.layout == kLayoutBCHW) {  // lane = channel * 8 + row * 2 + half
+      const int ch = lane >> 3, row = (lane >> 1) & 3, half = lane & 1;
+      dst = a.image + pix_index(kLayoutBCHW, b, ch, x0 + 4 * half, y0 + row, a.W, a.H);
+    } else {  // lane = row * 6 + q: floats 4q..4q+3 of the row's 24
+      const int row = lane / 6, q = lane - 6 * row;
+      dst = a.image + pix_index(kLayoutBHWC, b, 0, x0, y0 + row, a.W, a.H) + 4 * q;
+    }
+    *reinterpret_cast<float4*>(dst) = v;
+  }
+}
+
 // One global atomic per nonzero (triangle, parameter) accumulator of a list.
 template <class S>
 __device__ __forceinline__ void flush_grads(const S& sm, const RasterArgs& a, int b, int count) {
@@ -1216,6 +1211,28 @@ __device__ __forceinline__ float block_factor(const float4& s0, const float4& s1
   return zn >= 0 ? __int_as_float(0x7fc00000) : (z0 >= 0 ? 0.0f : ldexpf(s0.w, -64 * e));
 }
 
+// k-th index of 0..n-1 in centre-out order: c, c-1, c+1, c-2, c+2, ...
+__device__ __forceinline__ int center_out(int k, int n) {
+  const int c = (n - 1) >> 1, j = (k + 1) >> 1;
+  const int idx = (k & 1) ? c - j : c + j;
+  return idx < 0 ? c + j : idx;
+}
+
+// The (scene, tile) a tile-kernel CTA works on. The grid's x-y plane is read
+// as one linear index in launch order, scenes fastest and tiles centre-out
+// (central rows and columns first): the tiles with the most overlapping
+// geometry start first and the light border tiles fill the end of the launch,
+// which shortens its tail when there are only a few waves of CTAs (a small
+// batch, e.g. one rank's share of a batch split over GPUs).
+__device__ __forceinline__ void tile_of_block(const RasterArgs& a, int& b, int& local_tile) {
+  const unsigned lin = blockIdx.x + blockIdx.y * gridDim.x;
+  b = (int)(lin % (unsigned)a.B);
+  const int rank = (int)(lin / (unsigned)a.B);
+  const int cx = center_out(rank % a.tiles_x, a.tiles_x);
+  const int cy = center_out(rank / a.tiles_x, a.tile_rows);
+  local_tile = cy * a.tiles_x + cx;
+}
+
 // Tile kernel: one CTA per (scene, 16x16 tile[, triangle block]), warp w on
 // block w; lists longer than kChunk are binned in chunks behind barriers.
 template <int Mode, int kPrec>
@@ -1227,8 +1244,8 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   constexpr bool kSplit = Mode == kModeSplitFwd || kSplitBwd;
   constexpr bool kLoss = Mode == kModeLoss || Mode == kModeSplitBwd;
 
-  const int b = blockIdx.y;
-  const int local_tile = blockIdx.x;
+  int b, local_tile;
+  tile_of_block(a, b, local_tile);
   const int tile_col = local_tile % a.tiles_x;
   const int tile_row = a.tile_row0 + (local_tile / a.tiles_x) * a.tile_row_step;
   const int tx0 = tile_col * kTile, ty0 = tile_row * kTile;
@@ -1273,7 +1290,8 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
       }
       return;
     }
-    if (a.image && active) store_pixel(a, b, px, py, c0, c1, c2);
+    if (a.image) store_block(a, b, tx0 + (warp & 1) * kBlockW, ty0 + (warp >> 1) * kBlockH, lane,
+                             c0, c1, c2, sm.stage[warp]);
     if (Mode == kModeRender) return;
 
     // ---- loss and the gradient reaching the top of the stack --------------
@@ -1351,14 +1369,8 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   }
 
   if (kLoss && lead)
-    scene_loss(a, b, blockIdx.x, gridDim.x, sm.loss_part, kWarps, sm.loss_part, &sm.is_last);
-}
-
-// k-th index of 0..n-1 in centre-out order: c, c-1, c+1, c-2, c+2, ...
-__device__ __forceinline__ int center_out(int k, int n) {
-  const int c = (n - 1) >> 1, j = (k + 1) >> 1;
-  const int idx = (k & 1) ? c - j : c + j;
-  return idx < 0 ? c + j : idx;
+    scene_loss(a, b, local_tile, a.tiles_x * a.tile_rows, sm.loss_part, kWarps, sm.loss_part,
+               &sm.is_last);
 }
 
 // Region kernel, for scenes whose whole list fits one chunk (T <= kChunk):
@@ -1408,7 +1420,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArg
     Prod P;
     P.init();
     forward_walk<Mode, kPrec>(sm, count, blk, px, py, ptx, pty, active, K, c0, c1, c2, P);
-    if (a.image && active) store_pixel(a, b, px, py, c0, c1, c2);
+    if (a.image) store_block(a, b, x0, y0, lane, c0, c1, c2, sm.stage[warp]);
     if (Mode != kModeRender) {
       float G0, G1, G2;
       double sq;

@@ -371,3 +371,63 @@ def test_two_gpu_triangle_sharded_step_matches_one_gpu():
     p = torch.from_numpy(seed_scene_geometry(256, 1))[None].cuda()
     p[:, :, 6:9] = 0.5
     _check_against_one_gpu(res[0], p, target)
+
+
+def _leaving_worker(rank, world, port, out):
+    import datetime
+    import sys
+    import time
+
+    for p in (REPO, PKG):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    from diffrast import _native, sharded
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+
+    def fake(params, targets, sigma, shard, n_shards, background=(0.0, 0.0, 0.0), out=None):
+        grads, sums = out
+        grads.fill_(float(shard + 1))
+        sums.fill_(1.0)
+        return sums, grads
+
+    _native.loss_backward_sharded = fake
+    _native.adam_step = lambda *a, **k: None
+    step = sharded.ShardedSceneStep(torch.zeros(1, 3, 10))
+    tgt = torch.zeros(1, 4, 4, 3)
+    step.step(tgt, 0.01)  # step 1: both ranks
+    if rank == 1:
+        out[1] = "left"
+        os._exit(0)  # leaves between steps: no more collectives, no teardown
+    t0 = time.monotonic()
+    try:
+        step.step(tgt, 0.01)  # step 2: the peer is gone
+        out[0] = ("no error", time.monotonic() - t0)
+    except Exception as e:  # the collective ends with an error
+        out[0] = (type(e).__name__, time.monotonic() - t0)
+    os._exit(0)
+
+
+def test_a_departed_peer_ends_the_next_step_with_an_error():
+    # SURVEY's failure detection on the host: a rank that leaves between steps
+    # (no kernel or collective of its own in flight) must make the others'
+    # next collective fail within the process group's timeout, not hang.
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, out)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(90)
+            assert p.exitcode == 0
+        assert out[1] == "left"
+        kind, waited = out[0]
+    assert kind != "no error"
+    assert waited < 30.0
