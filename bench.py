@@ -176,13 +176,17 @@ def cpu_reference_rate(params, target, threads: int = 0, max_scenes: int = B,
     oracle.build()
     p, t = params[:max_scenes], target[:max_scenes]
     steps = 0
+    per = []
     t0 = time.perf_counter()
     while steps < max_steps:
+        ts = time.perf_counter()
         oracle.backward_batch(p, t, SIGMA, threads=threads)
+        per.append(time.perf_counter() - ts)
         steps += 1
         if time.perf_counter() - t0 >= min_seconds:
             break
     dt = time.perf_counter() - t0
+    cpu_reference_rate.step_ms = [1e3 * min(per), 1e3 * statistics.median(per), 1e3 * max(per)]
     return steps * dense_pairs(p.shape[0]) / dt, dt, p.shape[0], steps
 
 
@@ -500,6 +504,7 @@ def run_reference(args, rank: int, world: int):
         oracle.backward_batch(p_s, t_s, SIGMA, threads=threads)
         times.append(time.perf_counter() - t0)
     ms = 1e3 * statistics.mean(times)
+    spread = [1e3 * min(times), 1e3 * statistics.median(times), 1e3 * max(times)]
     value = dense_pairs(n) / (ms / 1e3)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -510,7 +515,8 @@ def run_reference(args, rank: int, world: int):
                    "global_batch": B, "seq_len": None, "parallelism": "cpu threads"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{n} of the {B} scenes per step (a full step takes "
-                                   f"{full:.2f} s), {args.steps} steps"},
+                                   f"{full:.2f} s), {args.steps} steps",
+                         "step_ms_min_median_max": spread, "host": host_identity()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference Rust crate cannot be built in this image (no cargo); timed the C++ "
                 "restatement of its CPU path (oracle/diffrast_oracle.cpp)",
@@ -737,6 +743,7 @@ def main():
                                     "sample": f"{nsteps} full steps of {ns} scenes ({dt:.1f} s "
                                               f"wall on {thr} threads), C++ restatement of the "
                                               "Rust CPU path",
+                                    "step_ms_min_median_max": cpu_reference_rate.step_ms,
                                     "calibration": calibration()}
         print(json.dumps(line), flush=True)
     if dist is not None:
