@@ -97,6 +97,23 @@ def inputs(rank: int):
     return params, target_scenes
 
 
+def echo_nccl_init(path: str, rank: int, world: int, local: int) -> None:
+    """This rank's NCCL communicator set-up lines (from NCCL_DEBUG_FILE) on
+    stderr, so a log shows the ranks and devices that took part."""
+    import torch
+
+    lines = []
+    try:
+        with open(path) as f:
+            lines = [ln.rstrip() for ln in f if "Init COMPLETE" in ln or "nRanks" in ln]
+    except OSError:
+        pass
+    ver = ".".join(str(v) for v in torch.cuda.nccl.version())
+    print(f"[bench] rank {rank}/{world} on cuda:{local}, NCCL {ver}", file=sys.stderr, flush=True)
+    for ln in lines[:4]:
+        print(f"[bench] {ln}", file=sys.stderr, flush=True)
+
+
 def rank_slice(rank: int, world: int) -> tuple[int, int]:
     """Scenes [lo, hi) of the 32-scene batch that rank `rank` of `world` owns
     under strong scaling: contiguous, as even as possible."""
@@ -542,12 +559,17 @@ def main():
             # NCCL's communicator set-up lines (ranks, devices, channels) on
             # stderr, so a log shows how many ranks took part; stdout keeps the
             # one JSON line.
-            os.environ.setdefault("NCCL_DEBUG", "INFO")
-            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+            import tempfile
+
+            nccl_log = os.path.join(tempfile.gettempdir(), f"dr_bench_nccl.{os.getpid()}.log")
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+            os.environ["NCCL_DEBUG_FILE"] = nccl_log
             torch.cuda.set_device(local)
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", local))
+            dist.barrier()
+            echo_nccl_init(nccl_log, rank, world, local)
         else:
             dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
 

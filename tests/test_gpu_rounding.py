@@ -7,7 +7,7 @@ about 2^-44 of the exact result, so it rounds like __fdiv_rn / __fsqrt_rn except
 for results that close to a rounding midpoint. sigmoid_rounded uses the fast
 exponential, whose documented error grows with the argument (2 + 1.16 |x|
 ulps); below zero the sigmoid is e / (1 + e) and inherits that error, above zero
-it is 1 / (1 + e) and hides it under the ulp of 1. The kernel evaluates the
+it is 1 / (1 + e), where that error moves 1 + e by at most an ulp or two. The kernel evaluates the
 sigmoid only for sd / sigma between about -14.2 (the reject line, ln(1e6) + 0.2)
 and 16.8 (the accept line); farther out the line tests decide the pair. The test
 bounds the sigmoid on that domain and reports the rest. The kernel is compiled here with nvcc from
@@ -99,5 +99,5 @@ def test_rounding_helpers_against_ieee():
     for name in ("div_rn_inv", "sqrt_nr"):
         assert res[name]["max_ulp"] <= 1, res
         assert res[name]["mismatches"] <= 1e-5 * N, res
-    assert res["sigmoid_rounded x >= 0"]["max_ulp"] <= 1, res
+    assert res["sigmoid_rounded x >= 0"]["max_ulp"] <= 2, res
     assert res["sigmoid_rounded x < 0 within 3 + 1.16|x| ulps"], res
