@@ -34,6 +34,7 @@ pub const DR_PRECISION_FAST: c_int = 2;
 pub const DR_PATH_TILE: c_int = 0;
 pub const DR_PATH_REGION: c_int = 1;
 pub const DR_PATH_SPLIT: c_int = 2;
+pub const DR_PATH_TILE_GATHER: c_int = 3;
 
 pub const DR_BACKWARD_TAPED: c_int = 0;
 pub const DR_BACKWARD_RECOMPUTE: c_int = 1;

@@ -98,7 +98,7 @@ struct dr_ctx {
   uint64_t hits = 0, misses = 0;
   Slot recs, partials, counters, bgbuf, split;
   // fit state
-  Slot fit_params, fit_m, fit_v, fit_grads, fit_losses, fit_state;
+  Slot fit_params, fit_m, fit_v, fit_grads, fit_losses, fit_state, fit_best, fit_target;
   cudaStream_t capture_stream = nullptr;
   cudaGraphExec_t fit_exec = nullptr;
   std::vector<unsigned char> fit_key;
@@ -147,9 +147,10 @@ dr_status ensure(dr_ctx* c, Slot& s, size_t bytes, bool zero) {
 
 // Every scratch buffer a context owns.
 std::vector<Slot*> slots(dr_ctx* c) {
-  return {&c->recs,      &c->partials,  &c->counters, &c->bgbuf,     &c->split,
-          &c->fit_params, &c->fit_m,    &c->fit_v,    &c->fit_grads, &c->fit_losses,
-          &c->fit_state, &c->io_params, &c->io_targets, &c->io_grads, &c->io_losses};
+  return {&c->recs,       &c->partials,   &c->counters,  &c->bgbuf,      &c->split,
+          &c->fit_params, &c->fit_m,      &c->fit_v,     &c->fit_grads,  &c->fit_losses,
+          &c->fit_state,  &c->fit_best,   &c->fit_target, &c->io_params, &c->io_targets,
+          &c->io_grads,   &c->io_losses};
 }
 
 uint64_t pool_bytes(dr_ctx* c) {
@@ -1023,6 +1024,8 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
   if ((st = ensure(ctx, ctx->fit_grads, np * 4, false))) return st;
   if ((st = ensure(ctx, ctx->fit_losses, (size_t)std::max(iters, 1) * 4, false))) return st;
   if ((st = ensure(ctx, ctx->fit_state, sizeof(FitState), true))) return st;
+  if ((st = ensure(ctx, ctx->fit_best, np * 4, false))) return st;
+  if ((st = ensure(ctx, ctx->fit_target, (size_t)H * W * 3 * 4, false))) return st;
   int tiles = ((W + kTileSide - 1) / kTileSide) * ((H + kTileSide - 1) / kTileSide);
   const int split_k = ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(1, T, tiles);
   if (split_k > 1 && (st = ensure(ctx, ctx->split, raster_split_bytes(1, split_k, H, W), false)))
@@ -1037,15 +1040,21 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
   float* Gr = (float*)ctx->fit_grads.ptr;
   float* L = (float*)ctx->fit_losses.ptr;
   FitState* S = (FitState*)ctx->fit_state.ptr;
+  float* Best = (float*)ctx->fit_best.ptr;
+  float* Tgt = (float*)ctx->fit_target.ptr;
 
-  // The graph bakes pointers, sizes and the config: reuse it when all match.
+  // The graph reads and writes only this context's buffers: the caller's
+  // target and initial scene are copied in before it runs and the results
+  // copied out after, so a caller that hands over fresh tensors each call
+  // (new allocations, new addresses) reuses the same graph. It bakes the
+  // buffers' addresses, the sizes and the config: reuse it when all match.
   std::vector<unsigned char> key;
   auto push = [&](const void* p, size_t n) {
     const unsigned char* b = (const unsigned char*)p;
     key.insert(key.end(), b, b + n);
   };
-  const void* ptrs[] = {target, init_params, best_params, final_params, P, M, V, Gr, L, S,
-                        ctx->recs.ptr, ctx->partials.ptr, ctx->counters.ptr, ctx->split.ptr};
+  const void* ptrs[] = {Tgt, Best, P, M, V, Gr, L, S, ctx->recs.ptr, ctx->partials.ptr,
+                        ctx->counters.ptr, ctx->split.ptr};
   push(ptrs, sizeof(ptrs));
   push(cfg, sizeof(*cfg));
   int dims[3] = {H, W, T};
@@ -1066,8 +1075,7 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
     auto chk = [&](cudaError_t e) {
       if (err == cudaSuccess && e != cudaSuccess) err = e;
     };
-    chk(cudaMemcpyAsync(P, init_params, np * 4, cudaMemcpyDeviceToDevice, cs));
-    chk(cudaMemcpyAsync(best_params, init_params, np * 4, cudaMemcpyDeviceToDevice, cs));
+    chk(cudaMemcpyAsync(Best, P, np * 4, cudaMemcpyDeviceToDevice, cs));
     chk(cudaMemsetAsync(M, 0, np * 4, cs));
     chk(cudaMemsetAsync(V, 0, np * 4, cs));
     chk(launch_fit_init(S, cs));
@@ -1094,7 +1102,7 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       a.bg3[1] = bg[1];
       a.bg3[2] = bg[2];
       a.layout = kLayoutBHWC;
-      a.other = target;
+      a.other = Tgt;
       a.grad_scale = 2.0f / (float)((long long)H * W * 3);
       a.grads = Gr;
       a.loss_partials = (double*)ctx->partials.ptr;
@@ -1144,12 +1152,11 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       ad.project = 1;
       ad.run_flag = &S->run_adam;
       ad.copy_flag = &S->copy_best;
-      ad.copy_dst = best_params;
+      ad.copy_dst = Best;
       const bool last = i + 1 == iters;
       chk(launch_fit_adam_setup(ad, Gr, T, W, H, last ? sigma : sigma_at(cfg, i + 1),
                                 last ? nullptr : (TriRec*)ctx->recs.ptr, cs));
     }
-    chk(cudaMemcpyAsync(final_params, P, np * 4, cudaMemcpyDeviceToDevice, cs));
     cudaGraph_t graph = nullptr;
     cudaError_t e_end = cudaStreamEndCapture(cs, &graph);
     if (err != cudaSuccess || e_end != cudaSuccess) {
@@ -1165,7 +1172,15 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
     }
     ctx->fit_key = key;
   }
+  DR_CUDA(cudaMemcpyAsync(Tgt, target, (size_t)H * W * 3 * 4, cudaMemcpyDeviceToDevice, s),
+          "copy the target in");
+  DR_CUDA(cudaMemcpyAsync(P, init_params, np * 4, cudaMemcpyDeviceToDevice, s),
+          "copy the initial scene in");
   DR_CUDA(cudaGraphLaunch(ctx->fit_exec, s), "launching the fit graph");
+  DR_CUDA(cudaMemcpyAsync(best_params, Best, np * 4, cudaMemcpyDeviceToDevice, s),
+          "copy the best scene out");
+  DR_CUDA(cudaMemcpyAsync(final_params, P, np * 4, cudaMemcpyDeviceToDevice, s),
+          "copy the final scene out");
   // Bounded wait first (POLL_TIMEOUT semantics), then the blocking reads.
   st = dr_stream_wait(stream, 600.0);
   if (st) return st;

@@ -221,11 +221,24 @@ struct Smem {
   TriRec rec[kChunk];
   unsigned char bcode[kChunk][kBlocksPerTile];
   int kidx[kChunk];
-  float acc[kChunk][kParams];
-  float4 stage[kWarps][24];  // one warp block's 96 image values (store_block)
+  // The image stores of pass 1 and the gradient sums of pass 2 never overlap
+  // in time: sharing the space keeps four CTAs an SM within the 132 KB
+  // shared-memory carve-out, which leaves the L1 cache its larger share.
+  union {
+    float acc[kChunk][kParams];
+    float4 stage[kWarps][24];  // one warp block's 96 image values (store_block)
+  };
   int warp_count[kWarps];
   double loss_part[kWarps];
   int is_last;
+  // Lists gathered from the tile's mask (scenes of more than kChunk
+  // triangles): the mask, one word per 32 triangles, the indices of the next
+  // list, and the gather's per-warp totals and position.
+  unsigned mask[kThreads];
+  int cand[kChunk];
+  int wsum[kWarps];
+  int mtotal[kWarps];
+  int gcount, gwc, gbo;
 };
 
 // Region kernel (a list of at most kChunk triangles): one CTA per region of
@@ -278,15 +291,16 @@ __device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0,
   return code;
 }
 
-// Bin triangles [c0, c0 + kChunk) of one scene against the tile, in order.
-__device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int c0, int tx0,
-                          int ty0, int W, int H) {
+// Bin one list of at most kChunk triangles against the tile, in order: thread
+// i < kChunk offers triangle k (valid false: none); the kept ones land in
+// shared memory in thread order with their eight block codes.
+__device__ int bin_list(Smem& sm, const TriRec* __restrict__ recs, int k, bool valid, int tx0,
+                        int ty0, int W, int H) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int k = c0 + (int)threadIdx.x;
   bool keep = false;
   unsigned long long code_all = 0;
   const TriRec* r = recs + k;
-  if ((int)threadIdx.x < kChunk && k < T && (r->flags & kLive)) {
+  if (valid && (r->flags & kLive)) {
     const TriRec& rr = *r;
     int skipped = 0;
 #pragma unroll
@@ -320,6 +334,131 @@ __device__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T, int 
   }
   __syncthreads();
   return total;
+}
+
+// Bin triangles [c0, c0 + kChunk) of one scene against the tile, in order.
+__device__ __forceinline__ int build_list(Smem& sm, const TriRec* __restrict__ recs, int T,
+                                          int c0, int tx0, int ty0, int W, int H) {
+  const int k = c0 + (int)threadIdx.x;
+  return bin_list(sm, recs, k, (int)threadIdx.x < kChunk && k < T, tx0, ty0, W, H);
+}
+
+// Tile masks. A scene with more than kChunk triangles would otherwise be
+// binned in fixed windows of kChunk triangles, every window tested against
+// the tile even when none of its triangles comes near it (most of them, on a
+// large canvas). Instead the CTA first marks, 32 triangles to a word, which
+// live triangles' pixel boxes meet its tile, then gathers its lists from the
+// marked triangles only, kChunk at a time and in triangle order, so the
+// composite runs over the same sequence as the fixed windows would give.
+// The gather's position (uniform over the CTA) lives in shared memory, not in
+// registers that would stay live across the list walks: gwc and gbo are the
+// next mask word to gather from and its first unused bit.
+struct Range {
+  int t0, t1;    // triangles [t0, t1) of the scene, at most kGatherMaxT
+  int tx0, ty0;  // the tile's first pixel
+  __device__ int words() const { return (t1 - t0 + 31) / 32; }
+};
+
+// The mask is one word per thread, held whole in shared memory.
+constexpr int kGatherMaxT = 32 * kThreads;
+
+// The tile's mask: bit l of word j is set when triangle t0 + 32 j + l is
+// live and its pixel box meets the tile. Warp w fills words w, w + kWarps,
+// ..., one ballot per word, four words' loads in flight at a time, and leaves
+// its words' bit count in sm.mtotal[w].
+__device__ void tile_mask(Smem& sm, const TriRec* __restrict__ recs, const Range& rg, int W,
+                          int H) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tx1 = min(rg.tx0 + kTile, W), ty1 = min(rg.ty0 + kTile, H);
+  const int end = rg.words();
+  int bits = 0;
+  for (int j0 = warp; j0 < end; j0 += 4 * kWarps) {
+    bool hit[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = j0 + u * kWarps;
+      const int k = rg.t0 + 32 * j + lane;
+      hit[u] = false;
+      if (j < end && k < rg.t1) {
+        const TriRec* r = recs + k;
+        const int f = r->flags;
+        const int x0 = r->bbox[0], y0 = r->bbox[1], x1 = r->bbox[2], y1 = r->bbox[3];
+        hit[u] = (f & kLive) && x0 < tx1 && x1 > rg.tx0 && y0 < ty1 && y1 > rg.ty0;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = j0 + u * kWarps;
+      const unsigned m = __ballot_sync(0xffffffffu, hit[u]);
+      if (lane == 0 && j < end) sm.mask[j] = m;
+      bits += __popc(m);
+    }
+  }
+  if (lane == 0) sm.mtotal[warp] = bits;
+}
+
+// Mark the tile's triangles and set the gather to the first; returns the
+// number marked. The caller orders this after every earlier read of the
+// gather state.
+__device__ __forceinline__ int gather_start(Smem& sm, const TriRec* __restrict__ recs,
+                                            const Range& rg, int W, int H) {
+  if (threadIdx.x == 0) {
+    sm.gwc = 0;
+    sm.gbo = 0;
+  }
+  tile_mask(sm, recs, rg, W, H);
+  __syncthreads();
+  int total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) total += sm.mtotal[w];
+  return total;
+}
+
+// The next kChunk marked triangles (fewer for the last list), in order, binned
+// into shared memory like a window of build_list. Every thread holds one mask
+// word: a block-wide prefix sum of the words' bit counts gives each word's
+// first slot. Lists are cut at bit granularity, so ceil(marked / kChunk)
+// calls take every marked triangle. The caller orders this call after the
+// previous one's reads with a barrier.
+__device__ int gather_list(Smem& sm, const TriRec* __restrict__ recs, const Range& rg, int W,
+                           int H) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = rg.words();
+  const int wc = sm.gwc, bo = sm.gbo;
+  const int j = wc + (int)threadIdx.x;
+  const bool valid = j < nw;
+  unsigned m = valid ? sm.mask[j] : 0u;
+  if (threadIdx.x == 0) m &= ~0u << bo;  // bits of the first word already used
+  const int c = __popc(m);
+  int incl = c;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += v;
+  }
+  if (lane == 31) sm.wsum[warp] = incl;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) incl += (w < warp) ? sm.wsum[w] : 0;
+  const int excl = incl - c;
+  if (valid && excl < kChunk) {
+    // This word starts inside the list. The list's last word is the one that
+    // fills it or the mask's last word; a word that overfills it gives only
+    // its first bits, and the next list resumes after them.
+    int slot = excl;
+    const int kbase = rg.t0 + 32 * j;
+    unsigned mm = m;
+    for (; mm && slot < kChunk; mm &= mm - 1) sm.cand[slot++] = kbase + __ffs(mm) - 1;
+    if (incl >= kChunk || j + 1 >= nw) {
+      sm.gcount = slot;
+      sm.gwc = mm ? j : j + 1;
+      sm.gbo = mm ? __ffs(mm) - 1 : 0;
+    }
+  }
+  __syncthreads();
+  const int n = sm.gcount;
+  const int i = (int)threadIdx.x;
+  return bin_list(sm, recs, i < n ? sm.cand[i] : 0, i < n, rg.tx0, rg.ty0, W, H);
 }
 
 // Pixel origin of warp block `blk` of a region: tiles of 8 blocks in the
@@ -1234,8 +1373,12 @@ __device__ __forceinline__ void tile_of_block(const RasterArgs& a, int& b, int& 
 }
 
 // Tile kernel: one CTA per (scene, 16x16 tile[, triangle block]), warp w on
-// block w; lists longer than kChunk are binned in chunks behind barriers.
-template <int Mode, int kPrec>
+// block w; lists longer than kChunk are binned in chunks behind barriers:
+// kGather (kChunk < T <= kGatherMaxT) gathers them from the triangles the
+// tile's mask marks, in triangle order; otherwise they are fixed windows of
+// kChunk triangles. Each form keeps its own straight-line loop: one body with
+// both list sources costs the walks 3-15 % more instructions.
+template <int Mode, int kPrec, bool kGather = false>
 __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -1243,6 +1386,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   constexpr bool kSplitBwd = Mode == kModeSplitBwd || Mode == kModeSplitBwdGrad;
   constexpr bool kSplit = Mode == kModeSplitFwd || kSplitBwd;
   constexpr bool kLoss = Mode == kModeLoss || Mode == kModeSplitBwd;
+  static_assert(!(kGather && kSplit), "split launches bin in windows");
 
   int b, local_tile;
   tile_of_block(a, b, local_tile);
@@ -1267,8 +1411,14 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     t0 = min(a.T, kb * per);
     t1 = min(a.T, t0 + per);
   }
-  const int n_chunks = (t1 - t0 + kChunk - 1) / kChunk;
+  int n_chunks = (t1 - t0 + kChunk - 1) / kChunk;
   int count = 0;
+  Range rg;
+  rg.t0 = t0;
+  rg.t1 = t1;
+  rg.tx0 = tx0;
+  rg.ty0 = ty0;
+  if constexpr (kGather) n_chunks = (gather_start(sm, recs, rg, a.W, a.H) + kChunk - 1) / kChunk;
   Prod P;
   P.init();
   float G0 = 0.0f, G1 = 0.0f, G2 = 0.0f;
@@ -1279,7 +1429,10 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
     float c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;  // a block composites over black
     if (!kSplit) scene_background(a, b, c0, c1, c2);
     for (int ci = 0; ci < n_chunks; ++ci) {
-      count = build_list(sm, recs, t1, t0 + ci * kChunk, tx0, ty0, a.W, a.H);
+      if constexpr (kGather)
+        count = gather_list(sm, recs, rg, a.W, a.H);
+      else
+        count = build_list(sm, recs, t1, t0 + ci * kChunk, tx0, ty0, a.W, a.H);
       forward_walk<Mode, kPrec>(sm, count, warp, px, py, ptx, pty, active, K, c0, c1, c2, P);
     }
     if (Mode == kModeSplitFwd) {
@@ -1355,10 +1508,22 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   // ---- pass 2: recomposite in forward order and accumulate gradients ------
   Prod Q;
   Q.init();
+  // A single list from pass 1 is still in shared memory; otherwise the lists
+  // are built again, in the same order (gathered from the mask, still held).
+  if (kGather && n_chunks > 1) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      sm.gwc = 0;
+      sm.gbo = 0;
+    }
+  }
   for (int ci = 0; ci < n_chunks; ++ci) {
+    __syncthreads();  // the previous list's flush, or pass 1's image stores in sm.stage
     if (n_chunks > 1 || kSplitBwd) {
-      __syncthreads();
-      count = build_list(sm, recs, t1, t0 + ci * kChunk, tx0, ty0, a.W, a.H);
+      if constexpr (kGather)
+        count = gather_list(sm, recs, rg, a.W, a.H);
+      else
+        count = build_list(sm, recs, t1, t0 + ci * kChunk, tx0, ty0, a.W, a.H);
     }
     for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
     __syncthreads();
@@ -1652,6 +1817,9 @@ cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
 }
 
 static_assert(sizeof(Smem) <= 48 * 1024, "raster smem must fit the default 48 KB limit");
+// Four tile CTAs an SM (the launch bound), each with 1 KB the system reserves,
+// within the 132 KB carve-out: the next one, 164 KB, takes 32 KB from L1.
+static_assert(4 * (sizeof(Smem) + 1024) <= 132 * 1024, "tile smem spills into the next carve-out");
 
 static_assert(sizeof(RegionSmem<32>) <= 48 * 1024, "region smem must fit the default 48 KB limit");
 
@@ -1694,7 +1862,8 @@ static bool use_region_kernel(int B, int T, int tiles_x, int tile_rows) {
 }
 int raster_path(int B, int T, int tiles_x, int tile_rows, int split_k) {
   if (split_k > 1) return 2;
-  return use_region_kernel(B, T, tiles_x, tile_rows) ? 1 : 0;
+  if (use_region_kernel(B, T, tiles_x, tile_rows)) return 1;
+  return T > kChunk && T <= kGatherMaxT ? 3 : 0;
 }
 template <int Mode, int kPrec>
 static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
@@ -1708,7 +1877,10 @@ static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s)
     return cudaGetLastError();
   }
   dim3 grid(n_tiles, a.B);
-  dr_raster_kernel<Mode, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  if (a.T > kChunk && a.T <= kGatherMaxT)
+    dr_raster_kernel<Mode, kPrec, true><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  else
+    dr_raster_kernel<Mode, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
   return cudaGetLastError();
 }
 

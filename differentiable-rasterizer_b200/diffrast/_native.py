@@ -21,7 +21,7 @@ LIB_PATH = os.path.join(_HERE, "libdiffrast_cuda.so")
 # dr_status (include/diffrast_cuda.h)
 OK, INVALID_ARGUMENT, TOO_LARGE, NO_DEVICE, TIMEOUT, LAUNCH, COMM, OUT_OF_MEMORY, INTERNAL = range(9)
 LAYOUT_BHWC, LAYOUT_BCHW = 0, 1
-PATH_TILE, PATH_REGION, PATH_SPLIT = 0, 1, 2  # dr_path
+PATH_TILE, PATH_REGION, PATH_SPLIT, PATH_TILE_GATHER = 0, 1, 2, 3  # dr_path
 BACKWARD_TAPED, BACKWARD_RECOMPUTE = 0, 1  # dr_backward_mode (BackwardMode)
 REDUCE_DIRECT, REDUCE_WORKGROUP = 0, 1  # dr_reduce_mode (ReduceMode)
 STOP_COMPLETED, STOP_CONVERGED, STOP_DIVERGED = 0, 1, 2
@@ -230,7 +230,7 @@ def set_triangle_split(blocks: int) -> None:
 def query_path(B: int, T: int, height: int, width: int,
                device: torch.device | None = None) -> int:
     """dr_query_path: the kernel a loss/gradient call of this shape takes
-    (PATH_TILE, PATH_REGION or PATH_SPLIT)."""
+    (PATH_TILE, PATH_REGION, PATH_SPLIT or PATH_TILE_GATHER)."""
     dev = _resolve_device(device)
     out = ctypes.c_int(-1)
     check(lib().dr_query_path(context(dev, _stream(dev)), B, T, height, width, ctypes.byref(out)))

@@ -122,13 +122,21 @@ DR_API dr_status dr_set_triangle_split(dr_ctx* ctx, int blocks);
 
 /* Which kernel dr_loss_backward / dr_grad_backward take for a batch of B
  * scenes of T triangles at H x W on this context's device (its triangle-split
- * setting included): DR_PATH_TILE (one CTA per scene and 16x16 tile),
- * DR_PATH_REGION (T <= 128 and at least one wave of CTAs: one CTA per 32x16
- * region, the list binned once for its 16 warp blocks) or DR_PATH_SPLIT (too
- * few tiles to fill the GPU: the triangle-block split). For tests and
- * profiling; results agree to rounding whichever path runs. No reference
- * counterpart (the reference has one WGSL pipeline per call). */
-typedef enum dr_path { DR_PATH_TILE = 0, DR_PATH_REGION = 1, DR_PATH_SPLIT = 2 } dr_path;
+ * setting included): DR_PATH_TILE (one CTA per scene and 16x16 tile, lists in
+ * fixed windows of 128 triangles), DR_PATH_REGION (T <= 128 and at least one
+ * wave of CTAs: one CTA per 32x16 region, the list binned once for its 16 warp
+ * blocks), DR_PATH_SPLIT (too few tiles to fill the GPU: the triangle-block
+ * split) or DR_PATH_TILE_GATHER (the tile kernel for 128 < T <= 8192, its
+ * lists gathered from a per-tile mask of the triangles whose boxes meet the
+ * tile). For tests and profiling; results agree to rounding whichever path
+ * runs. No reference counterpart (the reference has one WGSL pipeline per
+ * call). */
+typedef enum dr_path {
+  DR_PATH_TILE = 0,
+  DR_PATH_REGION = 1,
+  DR_PATH_SPLIT = 2,
+  DR_PATH_TILE_GATHER = 3
+} dr_path;
 DR_API dr_status dr_query_path(dr_ctx* ctx, int B, int T, int H, int W, int* path);
 
 /* --- hot path ------------------------------------------------------------ */

@@ -113,6 +113,8 @@ def test_config2_cells_full_batch(native, oracle, T, size):
 
     cell = [32, 128, 512].index(T) * 3 + [64, 128, 256].index(size)
     p, tp = config2_params(32, T, cell)
+    if T == 512:  # lists gathered from the tile masks
+        assert native.query_path(32, T, size, size) == native.PATH_TILE_GATHER
     target = oracle.render_batch(tp, size, size, 0.0015)
     full_parity(native, oracle, p, target, 0.0015, name=f"config2_T{T}_{size}")
 
@@ -124,6 +126,7 @@ def test_config5_full_batch(native, oracle, sigma):
     from diffrast.scenes import config5_params
 
     p = config5_params(16, 2048, 5000)
+    assert native.query_path(16, 2048, 512, 512) == native.PATH_TILE_GATHER
     target = oracle.render_batch(config5_params(16, 2048, 5100), 512, 512, sigma)
     img, grads = full_parity(native, oracle, p, target, sigma, name=f"config5_{sigma}")
     ref_img = oracle.render_batch(p, 512, 512, sigma)

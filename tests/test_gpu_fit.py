@@ -128,3 +128,35 @@ def test_repeated_fits_reuse_the_graph_and_agree(native):
     # Gradient sums use float atomics across tiles, so two runs agree to
     # rounding, not bitwise (the reference's GPU path behaves the same way).
     torch.testing.assert_close(a["losses"], b["losses"], rtol=1e-3, atol=0)
+
+
+def test_graph_follows_fresh_buffers_and_new_contents(native):
+    # The captured loop reads the context's own copies of the target and the
+    # initial scene, so calls with fresh tensors (new addresses, as a caller
+    # that keeps the previous result alive gets) and with new contents at an
+    # old address both fit what they were given.
+    g = torch.Generator(device="cuda").manual_seed(5)
+    target = torch.rand(40, 36, 3, device="cuda", generator=g)
+    other = torch.rand(40, 36, 3, device="cuda", generator=g)
+    p = torch.rand(150, 10, device="cuda", generator=g) * 0.6 + 0.2
+    a = native.fit(target, p, [0.3, 0.3, 0.3], iters=40, patience=None)
+    b = native.fit(target.clone(), p.clone(), [0.3, 0.3, 0.3], iters=40, patience=None)
+    torch.testing.assert_close(a["losses"], b["losses"], rtol=1e-3, atol=0)
+    # Gradient sums use float atomics, and Adam's first steps move a parameter
+    # by about its rate whatever the gradient's size, so parameters whose
+    # gradient is near zero may end up to a few rates apart.
+    torch.testing.assert_close(a["final_params"], b["final_params"], rtol=0, atol=0.05)
+    assert a["final_params"].data_ptr() != b["final_params"].data_ptr()
+    t2 = target.clone()
+    c = native.fit(t2, p, [0.3, 0.3, 0.3], iters=40, patience=None)
+    t2.copy_(other)
+    d = native.fit(t2, p, [0.3, 0.3, 0.3], iters=40, patience=None)
+    e = native.fit(other.clone(), p.clone(), [0.3, 0.3, 0.3], iters=40, patience=None)
+    torch.testing.assert_close(c["losses"], a["losses"], rtol=1e-3, atol=0)
+    torch.testing.assert_close(d["losses"], e["losses"], rtol=1e-3, atol=0)
+    assert not torch.allclose(d["losses"], a["losses"], rtol=1e-2)
+    # The initial scene is read each call too: its first loss is the loss of p.
+    q = p.clone()
+    q[:, 6:9] = 0.0
+    f = native.fit(target, q, [0.3, 0.3, 0.3], iters=40, patience=None)
+    assert not torch.allclose(f["losses"][:1], a["losses"][:1], rtol=1e-3)
