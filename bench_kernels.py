@@ -16,6 +16,13 @@ launch of each kernel (``-c 3``) sees the same work.
 ``--fit-iters N`` instead runs the config 1 fit (150 triangles, 176x176) for
 N iterations through ``dr_fit`` (one CUDA graph) twice, and prints the second
 run's time per iteration: a short driver for the fit graph's launch list.
+
+``--config C`` instead runs ``--steps`` loss + backward calls of one benchmark
+configuration whose scenes take the tile kernel's gathered lists (C = 4: one
+1024^2 scene of 4096 triangles; 5: 16 scenes of 2048 triangles at 512^2;
+2-512: 32 scenes of 512 triangles at 256^2; all at sigma 0.0015), after one
+render of the target: a short driver for an ncu capture of the raster kernel
+(skip the first raster launch, the target's render).
 """
 
 from __future__ import annotations
@@ -63,9 +70,14 @@ def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--fit-iters", type=int, default=0)
+    ap.add_argument("--config", choices=("4", "5", "2-512"))
+    ap.add_argument("--steps", type=int, default=3)
     args = ap.parse_args(argv)
     if args.fit_iters > 0:
         fit_graph(args.fit_iters)
+        return
+    if args.config:
+        config_steps(args.config, args.steps)
         return
     peak, src = _peak_gbs()
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -101,6 +113,23 @@ def main(argv=None) -> None:
 
     ms = _time(adam, args.reps)
     line("dr_adam_kernel", 28 * npar, ms, f"{npar} parameters")
+
+
+def config_steps(config: str, steps: int) -> None:
+    from diffrast import scenes as S
+
+    if config == "4":
+        p, tp, size = S.config4_params(4096, 4000), S.config4_params(4096, 4001), 1024
+    elif config == "5":
+        p, tp, size = S.config5_params(16, 2048, 5000), S.config5_params(16, 2048, 5100), 512
+    else:
+        (p, tp), size = S.config2_params(32, 512, 8), 256
+    P = torch.from_numpy(p).cuda()
+    target = _native.render(torch.from_numpy(tp).cuda(), size, size, 0.0015)
+    path = _native.query_path(P.shape[0], P.shape[1], size, size)
+    ms = [_time(lambda: _native.loss_backward(P, target, 0.0015), 1) for _ in range(steps)]
+    print(json.dumps({"config": config, "B": P.shape[0], "T": P.shape[1], "size": size,
+                      "path": path, "ms_per_call": ms}), flush=True)
 
 
 def fit_graph(iters: int) -> None:
