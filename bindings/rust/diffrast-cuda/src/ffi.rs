@@ -171,6 +171,8 @@ extern "C" {
                        image: *mut c_float, stream: dr_stream_t) -> dr_status;
     pub fn dr_set_reduce_mode(ctx: *mut dr_ctx, mode: c_int) -> dr_status;
     pub fn dr_get_reduce_mode(ctx: *mut dr_ctx, mode: *mut c_int) -> dr_status;
+    pub fn dr_set_deterministic(ctx: *mut dr_ctx, on: c_int) -> dr_status;
+    pub fn dr_get_deterministic(ctx: *mut dr_ctx, on: *mut c_int) -> dr_status;
     pub fn dr_loss_backward_timed(ctx: *mut dr_ctx, params: *const c_float,
                                   background: *const c_float, bg_per_scene: c_int, b: c_int,
                                   t: c_int, h: c_int, w: c_int, sigma: c_float,

@@ -416,6 +416,25 @@ impl GpuRasterizer {
         Ok(split(losses, grads, n_tris))
     }
 
+    /// Deterministic gradient sums on this rasterizer (off by default): every
+    /// later gradient call, and `fit` through it, gives bit-identical gradients
+    /// call to call (fixed-point accumulation; `dr_set_deterministic`). No
+    /// reference counterpart.
+    pub fn set_deterministic(&self, on: bool) -> Result<(), GpuError> {
+        let _g = self.calls.lock().expect("rasterizer mutex poisoned");
+        // SAFETY: ctx is live.
+        check(unsafe { ffi::dr_set_deterministic(self.ctx.raw(), on as c_int) })
+    }
+
+    /// Whether [`Self::set_deterministic`] is on.
+    pub fn deterministic(&self) -> Result<bool, GpuError> {
+        let _g = self.calls.lock().expect("rasterizer mutex poisoned");
+        let mut on: c_int = 0;
+        // SAFETY: ctx is live; `on` is an out-pointer.
+        check(unsafe { ffi::dr_get_deterministic(self.ctx.raw(), &mut on) })?;
+        Ok(on != 0)
+    }
+
     /// As [`Self::backward_many`], with the phase breakdown. Phases run one
     /// after another, so this is slower; the breakdown is a diagnostic.
     pub fn backward_many_timed(&self, scenes: &[Scene], p: RenderParams, targets: &[Canvas])

@@ -95,8 +95,10 @@ struct dr_ctx {
   int precision = 0;
   int split_blocks = 0;  // dr_set_triangle_split: 0 automatic, 1 never, k exactly
   int reduce_mode = DR_REDUCE_WORKGROUP;  // dr_set_reduce_mode (both values: one reduction)
+  int deterministic = 0;                  // dr_set_deterministic
   uint64_t hits = 0, misses = 0;
   Slot recs, partials, counters, bgbuf, split;
+  Slot det_fx, det_nf;  // deterministic mode: fixed-point sums and non-finite flags
   // fit state
   Slot fit_params, fit_m, fit_v, fit_grads, fit_losses, fit_state, fit_best, fit_target;
   cudaStream_t capture_stream = nullptr;
@@ -148,9 +150,9 @@ dr_status ensure(dr_ctx* c, Slot& s, size_t bytes, bool zero) {
 // Every scratch buffer a context owns.
 std::vector<Slot*> slots(dr_ctx* c) {
   return {&c->recs,       &c->partials,   &c->counters,  &c->bgbuf,      &c->split,
-          &c->fit_params, &c->fit_m,      &c->fit_v,     &c->fit_grads,  &c->fit_losses,
-          &c->fit_state,  &c->fit_best,   &c->fit_target, &c->io_params, &c->io_targets,
-          &c->io_grads,   &c->io_losses};
+          &c->det_fx,     &c->det_nf,     &c->fit_params, &c->fit_m,     &c->fit_grads,
+          &c->fit_v,      &c->fit_losses, &c->fit_state,  &c->fit_best,  &c->fit_target,
+          &c->io_params,  &c->io_targets, &c->io_grads,   &c->io_losses};
 }
 
 uint64_t pool_bytes(dr_ctx* c) {
@@ -249,6 +251,23 @@ dr_status loss_scratch(dr_ctx* ctx, RasterArgs& a, int n_tiles) {
   return DR_OK;
 }
 
+// Deterministic mode's scratch for n_tris (scene, triangle) pairs, cleared on
+// the stream (the finalize leaves it clear too; this also covers a call that
+// failed half way). Sets the launch's fixed-point pointers; off: leaves them null.
+dr_status det_scratch(dr_ctx* ctx, RasterArgs& a, size_t n_tris, cudaStream_t s) {
+  if (!ctx->deterministic || n_tris == 0) return DR_OK;
+  dr_status st = ensure(ctx, ctx->det_fx, n_tris * kParams * sizeof(long long), true);
+  if (st) return st;
+  st = ensure(ctx, ctx->det_nf, n_tris * sizeof(int), true);
+  if (st) return st;
+  DR_CUDA(cudaMemsetAsync(ctx->det_fx.ptr, 0, n_tris * kParams * sizeof(long long), s),
+          "clear fixed-point sums");
+  DR_CUDA(cudaMemsetAsync(ctx->det_nf.ptr, 0, n_tris * sizeof(int), s), "clear flags");
+  a.grads_fx = (long long*)ctx->det_fx.ptr;
+  a.grads_nf = (int*)ctx->det_nf.ptr;
+  return DR_OK;
+}
+
 dr_status backward_common(dr_ctx* ctx, int mode, const float* params, const float* background,
                           int bg_per_scene, int B, int T, int H, int W, float sigma,
                           const float* other, int layout, int shard, int n_shards, float* grads,
@@ -290,14 +309,18 @@ dr_status backward_common(dr_ctx* ctx, int mode, const float* params, const floa
   // blocks (all tile rows only).
   const int k = n_shards > 1 ? 1
                 : ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(B, T, n_tiles);
+  if ((st = det_scratch(ctx, a, (size_t)B * T, s))) return st;
   if (k > 1) {
     st = ensure(ctx, ctx->split, raster_split_bytes(B, k, H, W), false);
     if (st) return st;
     DR_CUDA(launch_raster_split(mode, a, n_tiles, k, (float4*)ctx->split.ptr, s),
             "split raster kernels");
-    return DR_OK;
+  } else {
+    DR_CUDA(launch_raster(mode, a, n_tiles, s), "raster kernel");
   }
-  DR_CUDA(launch_raster(mode, a, n_tiles, s), "raster kernel");
+  if (a.grads_fx)
+    DR_CUDA(launch_det_finalize(a.grads_fx, a.grads_nf, grads, (long long)B * T * kParams, s),
+            "deterministic finalize");
   return DR_OK;
 }
 
@@ -574,6 +597,10 @@ dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params, const float* b
   if (split_at[nc] && (st = ensure(ctx, ctx->split, split_at[nc], false))) return st;
   if (per_scene && (st = ensure(ctx, ctx->bgbuf, sizeof(float) * 3 * (size_t)B, false)))
     return st;
+  if (ctx->deterministic && T > 0) {
+    if ((st = ensure(ctx, ctx->det_fx, per_p * B * sizeof(long long), true))) return st;
+    if ((st = ensure(ctx, ctx->det_nf, (size_t)T * B * sizeof(int), true))) return st;
+  }
   if (!ctx->io_copy) {
     // Created once per context; on a failure nothing half-made is kept.
     cudaStream_t q[3] = {};
@@ -613,6 +640,13 @@ dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params, const float* b
     chk(cudaMemcpyAsync(ctx->bgbuf.ptr, background, sizeof(float) * 3 * (size_t)B,
                         cudaMemcpyHostToDevice, ctx->io_copy),
         "uploading backgrounds");
+  const bool det = ctx->deterministic && T > 0;
+  if (det) {  // cleared ahead of the uploads, which every chunk waits for
+    chk(cudaMemsetAsync(ctx->det_fx.ptr, 0, per_p * B * sizeof(long long), ctx->io_copy),
+        "clearing fixed-point sums");
+    chk(cudaMemsetAsync(ctx->det_nf.ptr, 0, (size_t)T * B * sizeof(int), ctx->io_copy),
+        "clearing flags");
+  }
   // Every upload is queued first: a download into pageable memory blocks the
   // host thread, and must not hold back later chunks' uploads.
   for (int c = 0; c < nc; ++c) {
@@ -649,12 +683,19 @@ dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params, const float* b
     a.losses = L + l;
     a.loss_partials = (double*)ctx->partials.ptr + l * tiles;
     a.loss_counters = (unsigned*)ctx->counters.ptr + l;
+    if (det) {
+      a.grads_fx = (long long*)ctx->det_fx.ptr + l * per_p;
+      a.grads_nf = (int*)ctx->det_nf.ptr + l * T;
+    }
     if (k[c] > 1)
       chk(launch_raster_split(kModeLoss, a, tiles, k[c],
                               (float4*)((char*)ctx->split.ptr + split_at[c]), q),
           "split raster kernels");
     else
       chk(launch_raster(kModeLoss, a, tiles, q), "raster kernel");
+    if (det)
+      chk(launch_det_finalize(a.grads_fx, a.grads_nf, G + l * per_p, (long long)n * per_p, q),
+          "deterministic finalize");
     if (T > 0)
       chk(cudaMemcpyAsync(grads + l * per_p, G + l * per_p, sizeof(float) * n * per_p,
                           cudaMemcpyDeviceToHost, q),
@@ -703,6 +744,26 @@ dr_status dr_get_reduce_mode(dr_ctx* ctx, int* mode) {
   return DR_OK;
 }
 
+dr_status dr_set_deterministic(dr_ctx* ctx, int on) {
+  if (!ctx) return fail(DR_INVALID_ARGUMENT, "null context");
+  if (on != 0 && on != 1) return fail(DR_INVALID_ARGUMENT, "deterministic must be 0 or 1, got %d", on);
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  ctx->deterministic = on;
+  if (ctx->fit_exec) {
+    cudaGraphExecDestroy(ctx->fit_exec);
+    ctx->fit_exec = nullptr;
+    ctx->fit_key.clear();
+  }
+  return DR_OK;
+}
+
+dr_status dr_get_deterministic(dr_ctx* ctx, int* on) {
+  if (!ctx || !on) return fail(DR_INVALID_ARGUMENT, "null pointer");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  *on = ctx->deterministic;
+  return DR_OK;
+}
+
 dr_status dr_loss_backward_timed(dr_ctx* ctx, const float* params, const float* background,
                                  int bg_per_scene, int B, int T, int H, int W, float sigma,
                                  const float* targets, int layout, float* grads, float* losses,
@@ -733,6 +794,10 @@ dr_status dr_loss_backward_timed(dr_ctx* ctx, const float* params, const float* 
   if (background && bg_per_scene &&
       (st = ensure(ctx, ctx->bgbuf, sizeof(float) * 3 * (size_t)B, false)))
     return st;
+  if (ctx->deterministic && T > 0) {
+    if ((st = ensure(ctx, ctx->det_fx, np * sizeof(long long), true))) return st;
+    if ((st = ensure(ctx, ctx->det_nf, (size_t)B * T * sizeof(int), true))) return st;
+  }
   timings->alloc_ms =
       (float)std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - a0)
           .count();
@@ -781,11 +846,16 @@ dr_status dr_loss_backward_timed(dr_ctx* ctx, const float* params, const float* 
     a.losses = L;
     a.loss_partials = (double*)ctx->partials.ptr;
     a.loss_counters = (unsigned*)ctx->counters.ptr;
+    if (err == cudaSuccess && det_scratch(ctx, a, (size_t)B * T, s) != DR_OK)
+      chk(cudaErrorUnknown, "clearing the deterministic sums");
     if (k > 1)
       chk(launch_raster_split(kModeLoss, a, tiles, k, (float4*)ctx->split.ptr, s),
           "split raster kernels");
     else
       chk(launch_raster(kModeLoss, a, tiles, s), "raster kernel");
+    if (a.grads_fx)
+      chk(launch_det_finalize(a.grads_fx, a.grads_nf, G, (long long)B * T * kParams, s),
+          "deterministic finalize");
     chk(cudaEventRecord(ev[2], s), "recording an event");
     // readback.
     if (T > 0)
@@ -1026,6 +1096,9 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
   if ((st = ensure(ctx, ctx->fit_state, sizeof(FitState), true))) return st;
   if ((st = ensure(ctx, ctx->fit_best, np * 4, false))) return st;
   if ((st = ensure(ctx, ctx->fit_target, (size_t)H * W * 3 * 4, false))) return st;
+  const bool det = ctx->deterministic != 0;
+  if (det && (st = ensure(ctx, ctx->det_fx, np * sizeof(long long), true))) return st;
+  if (det && (st = ensure(ctx, ctx->det_nf, (size_t)T * sizeof(int), true))) return st;
   int tiles = ((W + kTileSide - 1) / kTileSide) * ((H + kTileSide - 1) / kTileSide);
   const int split_k = ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(1, T, tiles);
   if (split_k > 1 && (st = ensure(ctx, ctx->split, raster_split_bytes(1, split_k, H, W), false)))
@@ -1053,8 +1126,9 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
     const unsigned char* b = (const unsigned char*)p;
     key.insert(key.end(), b, b + n);
   };
-  const void* ptrs[] = {Tgt, Best, P, M, V, Gr, L, S, ctx->recs.ptr, ctx->partials.ptr,
-                        ctx->counters.ptr, ctx->split.ptr};
+  const void* ptrs[] = {Tgt,           Best,          P, M, V, Gr, L, S, ctx->recs.ptr,
+                        ctx->partials.ptr, ctx->counters.ptr, ctx->split.ptr,
+                        det ? ctx->det_fx.ptr : nullptr, det ? ctx->det_nf.ptr : nullptr};
   push(ptrs, sizeof(ptrs));
   push(cfg, sizeof(*cfg));
   int dims[3] = {H, W, T};
@@ -1076,6 +1150,10 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       if (err == cudaSuccess && e != cudaSuccess) err = e;
     };
     chk(cudaMemcpyAsync(Best, P, np * 4, cudaMemcpyDeviceToDevice, cs));
+    if (det) {  // each iteration's finalize leaves them clear for the next
+      chk(cudaMemsetAsync(ctx->det_fx.ptr, 0, np * sizeof(long long), cs));
+      chk(cudaMemsetAsync(ctx->det_nf.ptr, 0, (size_t)T * sizeof(int), cs));
+    }
     chk(cudaMemsetAsync(M, 0, np * 4, cs));
     chk(cudaMemsetAsync(V, 0, np * 4, cs));
     chk(launch_fit_init(S, cs));
@@ -1115,10 +1193,15 @@ dr_status dr_fit(dr_ctx* ctx, const float* target, int H, int W, const float* in
       a.fit_patience = cfg->patience;
       a.fit_min_delta = cfg->min_delta;
       a.fit_iter = i;
+      if (det) {
+        a.grads_fx = (long long*)ctx->det_fx.ptr;
+        a.grads_nf = (int*)ctx->det_nf.ptr;
+      }
       if (split_k > 1)
         chk(launch_raster_split(kModeLoss, a, tiles, split_k, (float4*)ctx->split.ptr, cs));
       else
         chk(launch_raster(kModeLoss, a, tiles, cs));
+      if (det) chk(launch_det_finalize(a.grads_fx, a.grads_nf, Gr, (long long)np, cs));
       AdamArgs ad;
       memset(&ad, 0, sizeof(ad));
       ad.params = P;

@@ -20,6 +20,8 @@ constexpr float kMinWeight = 1e-6f;  // raster.rs:34 MIN_WEIGHT
 // Triangle record written once per (scene, triangle) by the set-up kernel and
 // staged into shared memory by the raster kernels. 44 words, 16-byte aligned.
 struct __align__(16) TriRec {
+  int bbox[4];    // x0 y0 x1 y1 of pixel_bounds (raster.rs:144-168); all 0 unless
+                  // kLive. First, so that a tile's mask pass reads one 16-byte word.
   float v[6];     // x0 y0 x1 y1 x2 y2 (raw params)
   float e[6];     // edge vectors b - a for edges (v0,v1), (v1,v2), (v2,v0)
   float len2[3];  // |e|^2 as the reference computes it (raster.rs:127)
@@ -28,7 +30,6 @@ struct __align__(16) TriRec {
   float margin;   // absolute slack on the edge-line tests, normalized units
   float n[6];     // unit inward edge normals (fast path only)
   float c[3];     // edge line offsets: l_i(p) = n_i . p + c_i
-  int bbox[4];    // x0 y0 x1 y1 of pixel_bounds (raster.rs:144-168)
   int flags;
   float il[3];    // 1 / len2 (0 when len2 <= 1e-20: t = 0, raster.rs:129-130)
   float rej;      // skip pixels with min edge-line distance below -rej

@@ -46,6 +46,11 @@ struct RasterArgs {
   int split_k;                // triangle blocks of a split launch (else 0)
   int split_base;             // first block of this launch (grid z adds to it)
   float4* split_state;        // per (block, scene, pixel): 2 float4 of forward state
+  // Deterministic gradient sums (dr_set_deterministic), else null: (B,T,10)
+  // fixed-point sums and one non-finite flag word per (scene, triangle), both
+  // zero on entry; launch_det_finalize turns them into `grads`.
+  long long* grads_fx;
+  int* grads_nf;
   // dr_fit only (B = 1): the CTA that completes the loss also runs Fitter::step's
   // bookkeeping for iteration fit_iter (fit.rs:243-288).
   FitState* fit;
@@ -97,6 +102,10 @@ size_t tri_rec_bytes();
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
                          int tape_semantics, TriRec* recs, cudaStream_t s);
 cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s);
+// Deterministic gradient sums: grads[i] from the fixed-point sum fx[i] and the
+// non-finite flags nf[i / 10], n = B * T * 10 values; fx and nf are left zero
+// for the next launch.
+cudaError_t launch_det_finalize(long long* fx, int* nf, float* grads, long long n, cudaStream_t s);
 // Which kernel a launch over B scenes of tiles_x x tile_rows tiles takes:
 // 0 the tile kernel, 1 the region kernel, 2 the triangle-block split (split_k > 1).
 int raster_path(int B, int T, int tiles_x, int tile_rows, int split_k);

@@ -109,6 +109,7 @@ __device__ __forceinline__ TriRec make_record(const float* __restrict__ params, 
   // w = alpha * cov <= alpha: an alpha at or below MIN_WEIGHT never paints.
   if (alpha <= kMinWeight) alpha_ok = false;
   if (has_box && alpha_ok) flags |= kLive;
+  if (!(flags & kLive)) r.bbox[0] = r.bbox[1] = r.bbox[2] = r.bbox[3] = 0;  // meets no tile
 
   // Edge vectors and squared lengths with the reference's rounding.
   for (int k = 0; k < 3; ++k) {
@@ -222,12 +223,13 @@ struct Smem {
   unsigned char bcode[kChunk][kBlocksPerTile];
   int kidx[kChunk];
   // The image stores of pass 1 and the gradient sums of pass 2 never overlap
-  // in time: sharing the space keeps four CTAs an SM within the 132 KB
-  // shared-memory carve-out, which leaves the L1 cache its larger share.
+  // in time, so they share the space.
   union {
     float acc[kChunk][kParams];
-    float4 stage[kWarps][24];  // one warp block's 96 image values (store_block)
+    long long acc64[kChunk][kParams];  // the same sums in fixed point (deterministic mode)
+    float4 stage[kWarps][24];          // one warp block's 96 image values (store_block)
   };
+  int nf[kChunk];  // deterministic mode: non-finite flags of the list's sums
   int warp_count[kWarps];
   double loss_part[kWarps];
   int is_last;
@@ -249,7 +251,11 @@ struct RegionSmem {
   TriRec rec[kChunk];
   unsigned char bcode[kChunk][kRB];
   int kidx[kChunk];
-  float acc[kChunk][kParams];
+  union {
+    float acc[kChunk][kParams];
+    long long acc64[kChunk][kParams];  // the same sums in fixed point (deterministic mode)
+  };
+  int nf[kChunk];  // deterministic mode: non-finite flags of the list's sums
   float4 stage[kWarps][24];  // one warp block's 96 image values (store_block)
   int warp_count[kWarps];
   double loss_part[kRB];
@@ -363,9 +369,10 @@ struct Range {
 constexpr int kGatherMaxT = 32 * kThreads;
 
 // The tile's mask: bit l of word j is set when triangle t0 + 32 j + l is
-// live and its pixel box meets the tile. Warp w fills words w, w + kWarps,
-// ..., one ballot per word, four words' loads in flight at a time, and leaves
-// its words' bit count in sm.mtotal[w].
+// live and its pixel box meets the tile (a triangle that is not live has an
+// empty box). Warp w fills words w, w + kWarps, ..., one ballot per word, four
+// words' 16-byte box loads in flight at a time, and leaves its words' bit count
+// in sm.mtotal[w].
 __device__ void tile_mask(Smem& sm, const TriRec* __restrict__ recs, const Range& rg, int W,
                           int H) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -380,10 +387,8 @@ __device__ void tile_mask(Smem& sm, const TriRec* __restrict__ recs, const Range
       const int k = rg.t0 + 32 * j + lane;
       hit[u] = false;
       if (j < end && k < rg.t1) {
-        const TriRec* r = recs + k;
-        const int f = r->flags;
-        const int x0 = r->bbox[0], y0 = r->bbox[1], x1 = r->bbox[2], y1 = r->bbox[3];
-        hit[u] = (f & kLive) && x0 < tx1 && x1 > rg.tx0 && y0 < ty1 && y1 > rg.ty0;
+        const int4 bb = *reinterpret_cast<const int4*>(recs[k].bbox);
+        hit[u] = bb.x < tx1 && bb.z > rg.tx0 && bb.y < ty1 && bb.w > rg.ty0;
       }
     }
 #pragma unroll
@@ -507,7 +512,12 @@ __device__ int build_region_list(RegionSmem<kRB>& sm, const RasterArgs& a,
   const bool keep = keep_half || partner_keeps;
   const unsigned ballot = __ballot_sync(0xffffffffu, keep && !half);  // one bit per triangle
   if (lane == 0) sm.warp_count[warp] = __popc(ballot);
-  for (int i = threadIdx.x; i < kChunk * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
+  if (a.grads_fx) {
+    for (int i = threadIdx.x; i < kChunk * kParams; i += kThreads) (&sm.acc64[0][0])[i] = 0;
+    for (int i = threadIdx.x; i < kChunk; i += kThreads) sm.nf[i] = 0;
+  } else {
+    for (int i = threadIdx.x; i < kChunk * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
+  }
   __syncthreads();
   int base = 0, total = 0;
 #pragma unroll
@@ -535,6 +545,7 @@ __device__ int build_region_list(RegionSmem<kRB>& sm, const RasterArgs& a,
 
 struct Consts {
   float sigma_eff, inv_sigma;
+  bool det;  // deterministic gradient sums (fixed point)
 };
 
 // Precision modes of the soft-edge (band) arithmetic.
@@ -1019,6 +1030,33 @@ __device__ __forceinline__ size_t pix_index(int layout, int b, int ch, int px, i
   return (((size_t)b * H + py) * W + px) * 3 + ch;
 }
 
+// Deterministic mode: a list's sums in 64-bit fixed point, 2^-36 resolution,
+// so that their value does not depend on the order of the atomic additions
+// (integer addition is associative). A warp total of magnitude 2^20 or more,
+// infinite or NaN, sets the parameter's bit in a flag word instead (NaN,
+// positive, negative: 3 bits per parameter), which the finalize turns into
+// NaN or an infinity, as the float sum of such values would be.
+constexpr float kDetScale = 68719476736.0f;      // 2^36
+constexpr float kDetInv = 1.4551915228366852e-11f;  // 2^-36
+constexpr float kDetLimit = 72057594037927936.0f;  // 2^56 = 2^20 * kDetScale
+__device__ __forceinline__ int nonfinite_bit(float v, int p) {
+  return 1 << (3 * p + (v != v ? 0 : (v > 0.0f ? 1 : 2)));
+}
+__device__ __forceinline__ void acc_add_fixed(unsigned long long* sum, int* flags, float v, int p) {
+  const float s = __fmul_rn(v, kDetScale);
+  if (fabsf(s) < kDetLimit)
+    atomicAdd(sum, (unsigned long long)__float2ll_rn(s));
+  else
+    atomicOr(flags, nonfinite_bit(v, p));
+}
+template <class S>
+__device__ __forceinline__ void acc_add(S& sm, int j, int p, float v, bool det) {
+  if (!det)
+    atomicAdd(&sm.acc[j][p], v);
+  else
+    acc_add_fixed(reinterpret_cast<unsigned long long*>(&sm.acc64[j][p]), &sm.nf[j], v, p);
+}
+
 // Pass 1 over a staged list for one lane's pixel: composites in order
 // (raster.rs:63) and keeps the running product of 1 - w. `col` selects the
 // warp's block code.
@@ -1148,14 +1186,14 @@ __device__ __forceinline__ void gradient_walk(S& sm, int count, int col, int lan
         const float v8[8] = {acc[0], acc[1], acc[2], acc[3], acc[6], acc[7], acc[8], acc[9]};
         const float sum = reduce8(v8, lane);
         const int prm = reduce8_param(lane, e1);
-        if (prm >= 0) atomicAdd(&sm.acc[j][prm], sum);
+        if (prm >= 0) acc_add(sm, j, prm, sum, K.det);
       } else {
         const float sum = reduce10(acc, lane);
-        if (slot10 >= 0) atomicAdd(&sm.acc[j][slot10], sum);
+        if (slot10 >= 0) acc_add(sm, j, slot10, sum, K.det);
       }
     } else {
       const float sum = reduce4(acc[6], acc[7], acc[8], acc[9], lane);
-      if ((lane & 7) == 0) atomicAdd(&sm.acc[j][6 + (lane >> 3)], sum);
+      if ((lane & 7) == 0) acc_add(sm, j, 6 + (lane >> 3), sum, K.det);
     }
   }
 }
@@ -1249,9 +1287,28 @@ __device__ __forceinline__ void store_block(const RasterArgs& a, int b, int x0, 
   }
 }
 
+// Deterministic mode's flush.
+__device__ __forceinline__ void flush_fixed(const long long* acc64, const int* nf, const int* kidx,
+                                         int count, long long* fx, int* nfg) {
+  for (int i = threadIdx.x; i < count * kParams; i += kThreads) {
+    const long long q = acc64[i];
+    if (q != 0)
+      atomicAdd(reinterpret_cast<unsigned long long*>(&fx[(size_t)kidx[i / kParams] * kParams +
+                                                           (i % kParams)]),
+                (unsigned long long)q);
+  }
+  for (int i = threadIdx.x; i < count; i += kThreads)
+    if (nf[i]) atomicOr(&nfg[kidx[i]], nf[i]);
+}
+
 // One global atomic per nonzero (triangle, parameter) accumulator of a list.
-template <class S>
+template <bool kDet, class S>
 __device__ __forceinline__ void flush_grads(const S& sm, const RasterArgs& a, int b, int count) {
+  if (kDet) {  // deterministic mode: fixed-point sums and flag words
+    flush_fixed(&sm.acc64[0][0], sm.nf, sm.kidx, count, a.grads_fx + (size_t)b * a.T * kParams,
+                a.grads_nf + (size_t)b * a.T);
+    return;
+  }
   float* g = a.grads + (size_t)b * a.T * kParams;
   for (int i = threadIdx.x; i < count * kParams; i += kThreads) {
     const float v = (&sm.acc[0][0])[i];
@@ -1378,7 +1435,7 @@ __device__ __forceinline__ void tile_of_block(const RasterArgs& a, int& b, int& 
 // tile's mask marks, in triangle order; otherwise they are fixed windows of
 // kChunk triangles. Each form keeps its own straight-line loop: one body with
 // both list sources costs the walks 3-15 % more instructions.
-template <int Mode, int kPrec, bool kGather = false>
+template <int Mode, int kPrec, bool kGather = false, bool kDet = false>
 __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -1402,6 +1459,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   Consts K;
   K.sigma_eff = a.sigma_eff;
   K.inv_sigma = a.inv_sigma;
+  K.det = kDet;  // deterministic sums (a.grads_fx set): a separate instantiation
   // Triangles [t0, t1): all of them, or block kb of a split launch.
   const int kb = a.split_base + (int)blockIdx.z;
   const bool lead = !kSplitBwd || blockIdx.z == 0;  // writes the image and the loss
@@ -1525,12 +1583,17 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
       else
         count = build_list(sm, recs, t1, t0 + ci * kChunk, tx0, ty0, a.W, a.H);
     }
-    for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
+    if (K.det) {
+      for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc64[0][0])[i] = 0;
+      for (int i = threadIdx.x; i < count; i += kThreads) sm.nf[i] = 0;
+    } else {
+      for (int i = threadIdx.x; i < count * kParams; i += kThreads) (&sm.acc[0][0])[i] = 0.0f;
+    }
     __syncthreads();
     gradient_walk<kPrec>(sm, count, warp, lane, px, py, ptx, pty, active, K, P, Q, G0, G1, G2, r0,
                          r1, r2);
     __syncthreads();
-    flush_grads(sm, a, b, count);
+    flush_grads<kDet>(sm, a, b, count);
   }
 
   if (kLoss && lead)
@@ -1543,7 +1606,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
 // region's warp blocks, warps taking blocks from a shared counter. A warp that
 // finishes a cheap block takes the next one instead of waiting for the CTA's
 // busiest warp; there is no barrier between the list and the final flush.
-template <int Mode, int kPrec, int kRows>
+template <int Mode, int kPrec, int kRows, bool kDet = false>
 __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArgs a) {
   constexpr int kRB = kRegionCols * kRows * kBlocksPerTile;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1567,6 +1630,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArg
   Consts K;
   K.sigma_eff = a.sigma_eff;
   K.inv_sigma = a.inv_sigma;
+  K.det = kDet;  // deterministic sums (a.grads_fx set): a separate instantiation
 
   if (threadIdx.x == 0) sm.next_block = kWarps;
   const int count = build_region_list(sm, a, a.recs + (size_t)b * a.T, rx0, lrow0);
@@ -1609,7 +1673,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArg
 
   if (Mode == kModeRender) return;
   __syncthreads();
-  flush_grads(sm, a, b, count);
+  flush_grads<kDet>(sm, a, b, count);
   if (Mode == kModeLoss)
     scene_loss(a, b, region, n_regions, sm.loss_part, kRB, sm.loss_part, &sm.is_last);
 }
@@ -1817,9 +1881,8 @@ cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
 }
 
 static_assert(sizeof(Smem) <= 48 * 1024, "raster smem must fit the default 48 KB limit");
-// Four tile CTAs an SM (the launch bound), each with 1 KB the system reserves,
-// within the 132 KB carve-out: the next one, 164 KB, takes 32 KB from L1.
-static_assert(4 * (sizeof(Smem) + 1024) <= 132 * 1024, "tile smem spills into the next carve-out");
+// Four CTAs an SM (the launch bound), each with the 1 KB the system reserves.
+static_assert(4 * (sizeof(Smem) + 1024) <= 227 * 1024, "four tile CTAs must fit an SM");
 
 static_assert(sizeof(RegionSmem<32>) <= 48 * 1024, "region smem must fit the default 48 KB limit");
 
@@ -1869,16 +1932,27 @@ template <int Mode, int kPrec>
 static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s) {
   constexpr int kRows = kRegionRows;
   constexpr int kRB = kRegionCols * kRows * kBlocksPerTile;
+  constexpr bool kGrads = Mode != kModeRender;
+  const bool det = kGrads && a.grads_fx != nullptr;
   const long long n_ctas = region_ctas(a.B, a.tiles_x, a.tile_rows);
   if (use_region_kernel(a.B, a.T, a.tiles_x, a.tile_rows)) {
     if (n_ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    dr_raster_region_kernel<Mode, kPrec, kRows>
-        <<<(unsigned)n_ctas, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);
+    const unsigned grid = (unsigned)n_ctas;
+    if (det)
+      dr_raster_region_kernel<Mode, kPrec, kRows, kGrads>
+          <<<grid, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);
+    else
+      dr_raster_region_kernel<Mode, kPrec, kRows><<<grid, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);
     return cudaGetLastError();
   }
   dim3 grid(n_tiles, a.B);
-  if (a.T > kChunk && a.T <= kGatherMaxT)
+  const bool gather = a.T > kChunk && a.T <= kGatherMaxT;
+  if (gather && det)
+    dr_raster_kernel<Mode, kPrec, true, kGrads><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  else if (gather)
     dr_raster_kernel<Mode, kPrec, true><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  else if (det)
+    dr_raster_kernel<Mode, kPrec, false, kGrads><<<grid, kThreads, sizeof(Smem), s>>>(a);
   else
     dr_raster_kernel<Mode, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
   return cudaGetLastError();
@@ -1910,8 +1984,14 @@ int raster_split_blocks(int B, int T, int n_tiles) {
 // for the loss or for an upstream image gradient.
 template <int kPrec>
 static cudaError_t launch_split_bwd(int mode, const RasterArgs& a, dim3 grid, cudaStream_t s) {
-  if (mode == kModeLoss)
+  const bool det = a.grads_fx != nullptr;
+  if (mode == kModeLoss && det)
+    dr_raster_kernel<kModeSplitBwd, kPrec, false, true><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  else if (mode == kModeLoss)
     dr_raster_kernel<kModeSplitBwd, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
+  else if (det)
+    dr_raster_kernel<kModeSplitBwdGrad, kPrec, false, true>
+        <<<grid, kThreads, sizeof(Smem), s>>>(a);
   else
     dr_raster_kernel<kModeSplitBwdGrad, kPrec><<<grid, kThreads, sizeof(Smem), s>>>(a);
   return cudaGetLastError();
@@ -1978,6 +2058,38 @@ cudaError_t launch_triangle_block(int phase, int mode, const RasterArgs& args, i
     case kPrecFast: return launch_block_prec<kPrecFast>(phase, mode, a, n_tiles, s);
   }
   return cudaErrorInvalidValue;
+}
+
+// Deterministic mode's last step, one thread per (scene, triangle): its ten
+// fixed-point sums to f32 (one rounding from the 64-bit integer, then an exact
+// power-of-two scale), or NaN / an infinity where a flag bit is set; the sums
+// and flags are cleared for the next launch.
+__global__ void dr_det_finalize_kernel(long long* __restrict__ fx, int* __restrict__ nf,
+                                       float* __restrict__ g, long long n_tris) {
+  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (t >= n_tris) return;
+  const int f = nf[t];
+  nf[t] = 0;
+#pragma unroll
+  for (int p = 0; p < kParams; ++p) {
+    const long long i = t * kParams + p;
+    const int bits = (f >> (3 * p)) & 7;
+    float v = __fmul_rn(__ll2float_rn(fx[i]), kDetInv);
+    if ((bits & 1) || (bits & 6) == 6) v = __int_as_float(0x7fc00000);
+    else if (bits & 2) v = __int_as_float(0x7f800000);
+    else if (bits & 4) v = __int_as_float(0xff800000);
+    g[i] = v;
+    fx[i] = 0;
+  }
+}
+
+cudaError_t launch_det_finalize(long long* fx, int* nf, float* grads, long long n, cudaStream_t s) {
+  const long long n_tris = n / kParams;
+  if (n_tris == 0) return cudaSuccess;
+  const long long blocks = (n_tris + 255) / 256;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  dr_det_finalize_kernel<<<(unsigned)blocks, 256, 0, s>>>(fx, nf, grads, n_tris);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_raster(int mode, const RasterArgs& args, int n_tiles, cudaStream_t s) {

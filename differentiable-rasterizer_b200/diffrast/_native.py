@@ -111,6 +111,8 @@ SIGNATURES = {
     "dr_backward": (_I, [_P, _P, _P, _I, _I, _I, _F, _P, _I, _I, _P, _P, _P, _P]),
     "dr_set_reduce_mode": (_I, [_P, _I]),
     "dr_get_reduce_mode": (_I, [_P, ctypes.POINTER(_I)]),
+    "dr_set_deterministic": (_I, [_P, _I]),
+    "dr_get_deterministic": (_I, [_P, ctypes.POINTER(_I)]),
     "dr_loss_backward_timed": (
         _I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P,
              ctypes.POINTER(BackwardTimingsC), _P]),
@@ -193,6 +195,8 @@ def context(device: torch.device, stream: int):
                     check(lib().dr_set_precision(h, _precision))
                 if _split:
                     check(lib().dr_set_triangle_split(h, _split))
+                if _deterministic:
+                    check(lib().dr_set_deterministic(h, 1))
                 _ctxs[key] = c = h
     return c
 
@@ -270,6 +274,23 @@ def get_reduce_mode(device: torch.device | None = None) -> int:
     out = ctypes.c_int(-1)
     check(lib().dr_get_reduce_mode(context(dev, _stream(dev)), ctypes.byref(out)))
     return out.value
+
+
+_deterministic = False
+
+
+def set_deterministic(on: bool) -> None:
+    """Deterministic gradient sums for every context (dr_set_deterministic):
+    bit-identical gradients call to call, fixed-point accumulation."""
+    global _deterministic
+    _deterministic = bool(on)
+    with _lock:
+        for h in _ctxs.values():
+            check(lib().dr_set_deterministic(h, int(_deterministic)))
+
+
+def get_deterministic() -> bool:
+    return _deterministic
 
 
 def shutdown() -> bool:

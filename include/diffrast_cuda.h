@@ -346,6 +346,21 @@ typedef enum dr_reduce_mode { DR_REDUCE_DIRECT = 0, DR_REDUCE_WORKGROUP = 1 } dr
 DR_API dr_status dr_set_reduce_mode(dr_ctx* ctx, int mode);
 DR_API dr_status dr_get_reduce_mode(dr_ctx* ctx, int* mode);
 
+/* Deterministic gradients (default off): with on = 1, every gradient call on
+ * this context (dr_loss_backward, dr_grad_backward, dr_backward,
+ * dr_loss_backward_sharded, dr_loss_backward_host, dr_loss_backward_timed and
+ * dr_fit) sums its per-warp contributions in 64-bit fixed point (2^-36
+ * resolution) instead of float atomics, so repeated calls, and repeated fits,
+ * give bit-identical gradients whatever the order the GPU adds them in. The
+ * sums are converted to f32 once at the end. A warp total of magnitude 2^20 or
+ * more, infinite or NaN makes that gradient NaN or an infinity (NaN when the
+ * signs disagree), as the float sum would. Costs one extra kernel per call and
+ * 10 KB more shared memory per CTA. dr_loss_backward_noalloc and the
+ * triangle-block entry points keep float atomics. No reference counterpart
+ * (the reference's sums are order-dependent too). */
+DR_API dr_status dr_set_deterministic(dr_ctx* ctx, int on);
+DR_API dr_status dr_get_deterministic(dr_ctx* ctx, int* on);
+
 /* BackwardTimings (diffrast-gpu/src/lib.rs:96-114): where the time of one
  * host-buffer loss + backward call went, in milliseconds.
  *   pack_ms      uploads of params, backgrounds and targets, plus the set-up
