@@ -3,7 +3,7 @@
 Prints one JSON line per kernel with its algorithmic bytes, CUDA-event time
 and achieved GB/s against the measured HBM peak. All sizes are far above the
 126 MB L2:
-- ``dr_setup_kernel``: 40 B of parameters read and one 176-byte record written
+- ``dr_setup_kernel``: 40 B of parameters read and one 160-byte record written
   per triangle. It is timed inside ``dr_render`` of 1x1 images, whose raster
   part is tiny; use ncu's per-kernel time for the kernel alone.
 - ``dr_mse_kernel`` (``dr_mse_loss``): two f32 images read.
@@ -20,9 +20,11 @@ run's time per iteration: a short driver for the fit graph's launch list.
 ``--config C`` instead runs ``--steps`` loss + backward calls of one benchmark
 configuration whose scenes take the tile kernel's gathered lists (C = 4: one
 1024^2 scene of 4096 triangles; 5: 16 scenes of 2048 triangles at 512^2;
-2-512: 32 scenes of 512 triangles at 256^2; all at sigma 0.0015), after one
-render of the target: a short driver for an ncu capture of the raster kernel
-(skip the first raster launch, the target's render).
+2-512: 32 scenes of 512 triangles at 256^2; 2-128: the headline cell, 128
+triangles at 256^2, whose first ``--batch`` scenes (default 32) are one
+rank's share under strong scaling; all at sigma 0.0015), after one render of
+the target: a short driver for an ncu capture of the raster kernel (skip the
+first raster launch, the target's render).
 """
 
 from __future__ import annotations
@@ -42,7 +44,7 @@ import torch  # noqa: E402
 
 from diffrast import _native  # noqa: E402
 
-REC_BYTES = 176
+REC_BYTES = 160
 
 
 def _peak_gbs() -> tuple[float, str]:
@@ -70,14 +72,15 @@ def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--fit-iters", type=int, default=0)
-    ap.add_argument("--config", choices=("4", "5", "2-512"))
+    ap.add_argument("--config", choices=("4", "5", "2-512", "2-128"))
+    ap.add_argument("--batch", type=int, default=32, help="scenes of config 2-128")
     ap.add_argument("--steps", type=int, default=3)
     args = ap.parse_args(argv)
     if args.fit_iters > 0:
         fit_graph(args.fit_iters)
         return
     if args.config:
-        config_steps(args.config, args.steps)
+        config_steps(args.config, args.steps, args.batch)
         return
     peak, src = _peak_gbs()
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -115,13 +118,16 @@ def main(argv=None) -> None:
     line("dr_adam_kernel", 28 * npar, ms, f"{npar} parameters")
 
 
-def config_steps(config: str, steps: int) -> None:
+def config_steps(config: str, steps: int, batch: int = 32) -> None:
     from diffrast import scenes as S
 
     if config == "4":
         p, tp, size = S.config4_params(4096, 4000), S.config4_params(4096, 4001), 1024
     elif config == "5":
         p, tp, size = S.config5_params(16, 2048, 5000), S.config5_params(16, 2048, 5100), 512
+    elif config == "2-128":
+        (p, tp), size = S.config2_params(32, 128, 5), 256
+        p, tp = p[:batch], tp[:batch]
     else:
         (p, tp), size = S.config2_params(32, 512, 8), 256
     P = torch.from_numpy(p).cuda()

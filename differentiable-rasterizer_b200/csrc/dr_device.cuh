@@ -18,28 +18,32 @@ constexpr float kMinWeight = 1e-6f;  // raster.rs:34 MIN_WEIGHT
 
 
 // Triangle record written once per (scene, triangle) by the set-up kernel and
-// staged into shared memory by the raster kernels. 44 words, 16-byte aligned.
-struct __align__(16) TriRec {
-  int bbox[4];    // x0 y0 x1 y1 of pixel_bounds (raster.rs:144-168); all 0 unless
-                  // kLive. First, so that a tile's mask pass reads one 16-byte word.
-  float v[6];     // x0 y0 x1 y1 x2 y2 (raw params)
-  float e[6];     // edge vectors b - a for edges (v0,v1), (v1,v2), (v2,v0)
-  float len2[3];  // |e|^2 as the reference computes it (raster.rs:127)
-  float alpha;    // clamp(a, 0, 1) (raster.rs:48)
-  float color[3];
-  float margin;   // absolute slack on the edge-line tests, normalized units
-  float n[6];     // unit inward edge normals (fast path only)
-  float c[3];     // edge line offsets: l_i(p) = n_i . p + c_i
-  int flags;
-  float il[3];    // 1 / len2 (0 when len2 <= 1e-20: t = 0, raster.rs:129-130)
-  float rej;      // skip pixels with min edge-line distance below -rej
-  float acc;      // w == alpha for pixels with min edge-line distance above acc
-  float wind;     // sign of the signed area (+1 / -1): the sign of the reference's
-                  // edge cross product on the inner side of every edge
-  float pad;
+// staged into shared memory by the raster kernels. 40 words, 16-byte aligned.
+// Each edge's data sits in one 32-byte run, so evaluating an edge whose index
+// the code knows loads two 16-byte words instead of eight scattered ones.
+struct __align__(16) EdgeRec {
+  float ax, ay;  // the edge's first vertex (raw params)
+  float ex, ey;  // edge vector b - a for edges (v0,v1), (v1,v2), (v2,v0)
+  float nx, ny;  // unit inward normal (fast path only)
+  float c;       // line offset: l(p) = n . p + c
+  float il;      // 1 / len2 (0 when len2 <= 1e-20: t = 0, raster.rs:129-130)
 };
-static_assert(sizeof(TriRec) == 176, "TriRec layout");
-constexpr int kRecWords = 44;
+struct __align__(16) TriRec {
+  int bbox[4];      // x0 y0 x1 y1 of pixel_bounds (raster.rs:144-168); all 0 unless
+                    // kLive. First, so that a tile's mask pass reads one 16-byte word.
+  EdgeRec ed[3];
+  float len2[3];    // |e|^2 as the reference computes it (raster.rs:127)
+  float alpha;      // clamp(a, 0, 1) (raster.rs:48)
+  float color[3];
+  float margin;     // absolute slack on the edge-line tests, normalized units
+  int flags;
+  float rej;        // skip pixels with min edge-line distance below -rej
+  float acc;        // w == alpha for pixels with min edge-line distance above acc
+  float wind;       // sign of the signed area (+1 / -1): the sign of the reference's
+                    // edge cross product on the inner side of every edge
+};
+static_assert(sizeof(TriRec) == 160, "TriRec layout");
+constexpr int kRecWords = 40;
 
 enum RecFlags : int {
   kLive = 1,         // has a non-empty box and a usable alpha
@@ -92,12 +96,12 @@ struct SdResult {
 // signed_distance + the nearest-edge bookkeeping of coverage_with_grad.
 // fminf ignores NaN like f32::min, so `sd` folds exactly as the reference;
 // the strict `<` walk picks the same edge value the fold lands on.
-__device__ __forceinline__ SdResult signed_distance_ref(const float* v, const float* e,
-                                                        const float* len2, float px, float py) {
+__device__ __forceinline__ SdResult signed_distance_ref(const EdgeRec* ed, const float* len2,
+                                                        float px, float py) {
   float t0, t1, t2, c0, c1, c2;
-  float d0 = segment_ref(v[0], v[1], e[0], e[1], len2[0], px, py, t0, c0);
-  float d1 = segment_ref(v[2], v[3], e[2], e[3], len2[1], px, py, t1, c1);
-  float d2 = segment_ref(v[4], v[5], e[4], e[5], len2[2], px, py, t2, c2);
+  float d0 = segment_ref(ed[0].ax, ed[0].ay, ed[0].ex, ed[0].ey, len2[0], px, py, t0, c0);
+  float d1 = segment_ref(ed[1].ax, ed[1].ay, ed[1].ex, ed[1].ey, len2[1], px, py, t1, c1);
+  float d2 = segment_ref(ed[2].ax, ed[2].ay, ed[2].ex, ed[2].ey, len2[2], px, py, t2, c2);
   float d = fminf(fminf(fminf(__int_as_float(0x7f800000), d0), d1), d2);
   SdResult r;
   int edge = 0;

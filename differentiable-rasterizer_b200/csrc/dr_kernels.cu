@@ -72,7 +72,10 @@ __device__ __forceinline__ TriRec make_record(const float* __restrict__ params, 
   float raw_alpha = p[9];
 
   TriRec r;
-  for (int j = 0; j < 6; ++j) r.v[j] = v[j];
+  for (int k = 0; k < 3; ++k) {
+    r.ed[k].ax = v[2 * k];
+    r.ed[k].ay = v[2 * k + 1];
+  }
   for (int j = 0; j < 3; ++j) r.color[j] = col[j];
   float alpha = rclamp(raw_alpha, 0.0f, 1.0f);
   r.alpha = alpha;
@@ -116,8 +119,8 @@ __device__ __forceinline__ TriRec make_record(const float* __restrict__ params, 
     int a = k, b = (k + 1) % 3;
     float ex = __fsub_rn(v[2 * b], v[2 * a]);
     float ey = __fsub_rn(v[2 * b + 1], v[2 * a + 1]);
-    r.e[2 * k] = ex;
-    r.e[2 * k + 1] = ey;
+    r.ed[k].ex = ex;
+    r.ed[k].ey = ey;
     r.len2[k] = __fadd_rn(__fmul_rn(ex, ex), __fmul_rn(ey, ey));
   }
 
@@ -128,7 +131,7 @@ __device__ __forceinline__ TriRec make_record(const float* __restrict__ params, 
   double area2 = ex0 * ey2 - ey0 * ex2;
   double maxl2 = 0.0, maxabs = 0.0;
   for (int k = 0; k < 3; ++k) {
-    double l2 = (double)r.e[2 * k] * r.e[2 * k] + (double)r.e[2 * k + 1] * r.e[2 * k + 1];
+    double l2 = (double)r.ed[k].ex * r.ed[k].ex + (double)r.ed[k].ey * r.ed[k].ey;
     maxl2 = fmax(maxl2, l2);
     maxabs = fmax(maxabs, fmax(fabs((double)v[2 * k]), fabs((double)v[2 * k + 1])));
   }
@@ -143,9 +146,9 @@ __device__ __forceinline__ TriRec make_record(const float* __restrict__ params, 
       len = 1.0;
     }
     double nx = s * -ey / len, ny = s * ex / len;
-    r.n[2 * k] = (float)nx;
-    r.n[2 * k + 1] = (float)ny;
-    r.c[k] = (float)(-(nx * v[2 * a] + ny * v[2 * a + 1]));
+    r.ed[k].nx = (float)nx;
+    r.ed[k].ny = (float)ny;
+    r.ed[k].c = (float)(-(nx * v[2 * a] + ny * v[2 * a + 1]));
   }
   // Slack for evaluating n.p + c in f32 and for the reference's own f32
   // distance rounding: a few ulps of the largest magnitude involved.
@@ -159,16 +162,15 @@ __device__ __forceinline__ TriRec make_record(const float* __restrict__ params, 
   const double lna = alpha > 0.0f ? log((double)alpha * 1e6) : 0.0;
   r.rej = (float)((fmax(lna, 0.0) + 0.2) * sig_eff) + r.margin;
   r.acc = (float)(16.8 * sig_eff) + r.margin;
-  for (int k = 0; k < 3; ++k) r.il[k] = r.len2[k] <= 1e-20f ? 0.0f : (float)(1.0 / (double)r.len2[k]);
+  for (int k = 0; k < 3; ++k) r.ed[k].il = r.len2[k] <= 1e-20f ? 0.0f : (float)(1.0 / (double)r.len2[k]);
   r.wind = (float)s;
-  r.pad = 0.0f;
   if (fast) flags |= kFastOk;
   r.flags = flags;
   return r;
 }
 
 // One thread per (scene, triangle). Records are staged in shared memory and
-// written as one contiguous run per block: a thread writing its own 176-byte
+// written as one contiguous run per block: a thread writing its own 160-byte
 // record would leave every 16-byte store to a different, partly written sector.
 constexpr int kSetupThreads = 128;
 __global__ void __launch_bounds__(kSetupThreads) dr_setup_kernel(
@@ -282,8 +284,8 @@ __device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0,
     int cand = 0;
 #pragma unroll
     for (int e = 0; e < 3; ++e) {
-      const float nx = r.n[2 * e], ny = r.n[2 * e + 1];
-      const float lc = __fmaf_rn(nx, cx, __fmaf_rn(ny, cy, r.c[e]));
+      const float nx = r.ed[e].nx, ny = r.ed[e].ny;
+      const float lc = __fmaf_rn(nx, cx, __fmaf_rn(ny, cy, r.ed[e].c));
       const float rad = __fmaf_rn(fabsf(nx), hx, __fmul_rn(fabsf(ny), hy));
       if (__fadd_rn(lc, rad) < -r.rej) return kBlkSkip;
       lmin_all = fminf(lmin_all, __fsub_rn(lc, rad));
@@ -579,9 +581,9 @@ struct PairEval {
 __device__ __forceinline__ void cov_grad_ref(const TriRec& r, int edge, float t, float dist,
                                              float cov, bool inside, float ptx, float pty,
                                              const Consts& K, PairEval& o) {
-  const float ax = r.v[2 * edge], ay = r.v[2 * edge + 1];
-  const float cpx = __fadd_rn(ax, __fmul_rn(t, r.e[2 * edge]));
-  const float cpy = __fadd_rn(ay, __fmul_rn(t, r.e[2 * edge + 1]));
+  const float ax = r.ed[edge].ax, ay = r.ed[edge].ay;
+  const float cpx = __fadd_rn(ax, __fmul_rn(t, r.ed[edge].ex));
+  const float cpy = __fadd_rn(ay, __fmul_rn(t, r.ed[edge].ey));
   const float rd = rcp_approx(dist);
   const float ux = div_rn_inv(__fsub_rn(ptx, cpx), dist, rd);
   const float uy = div_rn_inv(__fsub_rn(pty, cpy), dist, rd);
@@ -610,14 +612,14 @@ __device__ __noinline__ PairEval eval_ref(const TriRec* rp, float ptx, float pty
   PairEval o;
   o.edge = 0;
   o.dax = o.day = o.dbx = o.dby = 0.0f;
-  const SdResult g = signed_distance_ref(r.v, r.e, r.len2, ptx, pty);
+  const SdResult g = signed_distance_ref(r.ed, r.len2, ptx, pty);
   o.cov = sigmoid_ref(__fdiv_rn(g.sd, sigma_eff));
   o.w = __fmul_rn(r.alpha, o.cov);
   o.band = !(g.dist < 1e-9f);
   if (kGrad && o.band) {
-    const float ax = r.v[2 * g.edge], ay = r.v[2 * g.edge + 1];
-    const float cpx = __fadd_rn(ax, __fmul_rn(g.t, r.e[2 * g.edge]));
-    const float cpy = __fadd_rn(ay, __fmul_rn(g.t, r.e[2 * g.edge + 1]));
+    const float ax = r.ed[g.edge].ax, ay = r.ed[g.edge].ay;
+    const float cpx = __fadd_rn(ax, __fmul_rn(g.t, r.ed[g.edge].ex));
+    const float cpy = __fadd_rn(ay, __fmul_rn(g.t, r.ed[g.edge].ey));
     const float ux = __fdiv_rn(__fsub_rn(ptx, cpx), g.dist);
     const float uy = __fdiv_rn(__fsub_rn(pty, cpy), g.dist);
     float chain = __fdiv_rn(__fmul_rn(o.cov, __fsub_rn(1.0f, o.cov)), sigma_eff);
@@ -658,9 +660,9 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
   // side of every pixel of the block: they take no part in any decision.
   const int cand = code >> kCandShift;
   const float inf = __int_as_float(0x7f800000);
-  const float l0 = (cand & 1) ? __fmaf_rn(r.n[0], ptx, __fmaf_rn(r.n[1], pty, r.c[0])) : inf;
-  const float l1 = (cand & 2) ? __fmaf_rn(r.n[2], ptx, __fmaf_rn(r.n[3], pty, r.c[1])) : inf;
-  const float l2 = (cand & 4) ? __fmaf_rn(r.n[4], ptx, __fmaf_rn(r.n[5], pty, r.c[2])) : inf;
+  const float l0 = (cand & 1) ? __fmaf_rn(r.ed[0].nx, ptx, __fmaf_rn(r.ed[0].ny, pty, r.ed[0].c)) : inf;
+  const float l1 = (cand & 2) ? __fmaf_rn(r.ed[1].nx, ptx, __fmaf_rn(r.ed[1].ny, pty, r.ed[1].c)) : inf;
+  const float l2 = (cand & 4) ? __fmaf_rn(r.ed[2].nx, ptx, __fmaf_rn(r.ed[2].ny, pty, r.ed[2].c)) : inf;
   const float mn = fminf(fminf(l0, l1), l2);
   if (mn < -r.rej) return kSkip;
   if (mn > r.acc) {
@@ -687,9 +689,9 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
 #pragma unroll
   for (int e = 0; e < 3; ++e) {
     if (!(cand & (1 << e))) continue;
-    const float ex = r.e[2 * e], ey = r.e[2 * e + 1];
-    const float apx = __fsub_rn(ptx, r.v[2 * e]), apy = __fsub_rn(pty, r.v[2 * e + 1]);
-    const float te = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.il[e]));
+    const float ex = r.ed[e].ex, ey = r.ed[e].ey;
+    const float apx = __fsub_rn(ptx, r.ed[e].ax), apy = __fsub_rn(pty, r.ed[e].ay);
+    const float te = __saturatef(__fmul_rn(__fmaf_rn(apx, ex, __fmul_rn(apy, ey)), r.ed[e].il));
     const float dx = __fmaf_rn(-te, ex, apx), dy = __fmaf_rn(-te, ey, apy);
     const float d2 = __fmaf_rn(dx, dx, __fmul_rn(dy, dy));
     if (d2 < bd2) {
@@ -741,13 +743,13 @@ __device__ __forceinline__ int eval_pair(const TriRec& r, int code, int px, int 
 
   // kPrecRef: the nearest edge's segment distance exactly as
   // point_segment_distance computes it (raster.rs:124-134).
-  const float ax = r.v[2 * edge], ay = r.v[2 * edge + 1];
-  const float ex = r.e[2 * edge], ey = r.e[2 * edge + 1], len2 = r.len2[edge];
+  const float ax = r.ed[edge].ax, ay = r.ed[edge].ay;
+  const float ex = r.ed[edge].ex, ey = r.ed[edge].ey, len2 = r.len2[edge];
   const float apx = __fsub_rn(ptx, ax), apy = __fsub_rn(pty, ay);
   float t = 0.0f;
   if (!(len2 <= 1e-20f)) {
     const float dot = __fadd_rn(__fmul_rn(apx, ex), __fmul_rn(apy, ey));
-    t = rclamp(div_rn_inv(dot, len2, r.il[edge]), 0.0f, 1.0f);
+    t = rclamp(div_rn_inv(dot, len2, r.ed[edge].il), 0.0f, 1.0f);
   }
   const float dx = __fsub_rn(apx, __fmul_rn(t, ex));
   const float dy = __fsub_rn(apy, __fmul_rn(t, ey));
@@ -766,11 +768,11 @@ struct SegEval {
   float d, t, cross;
 };
 __device__ __forceinline__ SegEval seg_exact(const TriRec& r, int e, float ptx, float pty) {
-  const float ex = r.e[2 * e], ey = r.e[2 * e + 1], len2 = r.len2[e];
-  const float apx = __fsub_rn(ptx, r.v[2 * e]), apy = __fsub_rn(pty, r.v[2 * e + 1]);
+  const float ex = r.ed[e].ex, ey = r.ed[e].ey, len2 = r.len2[e];
+  const float apx = __fsub_rn(ptx, r.ed[e].ax), apy = __fsub_rn(pty, r.ed[e].ay);
   const float dot = __fadd_rn(__fmul_rn(apx, ex), __fmul_rn(apy, ey));
   SegEval o;
-  o.t = len2 <= 1e-20f ? 0.0f : rclamp(div_rn_inv(dot, len2, r.il[e]), 0.0f, 1.0f);
+  o.t = len2 <= 1e-20f ? 0.0f : rclamp(div_rn_inv(dot, len2, r.ed[e].il), 0.0f, 1.0f);
   const float dx = __fsub_rn(apx, __fmul_rn(o.t, ex));
   const float dy = __fsub_rn(apy, __fmul_rn(o.t, ey));
   o.d = sqrt_nr(__fadd_rn(__fmul_rn(dx, dx), __fmul_rn(dy, dy)));
@@ -809,7 +811,7 @@ __device__ __forceinline__ int eval_cand(const TriRec& r, int code, int cand, in
   for (int e = 0; e < 3; ++e) {
     cr[e] = r.wind;
     if (!(cand & (1 << e))) continue;
-    mn = fminf(mn, __fmaf_rn(r.n[2 * e], ptx, __fmaf_rn(r.n[2 * e + 1], pty, r.c[e])));
+    mn = fminf(mn, __fmaf_rn(r.ed[e].nx, ptx, __fmaf_rn(r.ed[e].ny, pty, r.ed[e].c)));
     const SegEval g = seg_exact(r, e, ptx, pty);
     cr[e] = g.cross;
     if (g.d < best) {
@@ -841,7 +843,7 @@ __device__ __forceinline__ int eval_single(const TriRec& r, int code, int px, in
   if (code & kBlkBox) {
     live = (px >= r.bbox[0]) & (px < r.bbox[2]) & (py >= r.bbox[1]) & (py < r.bbox[3]);
   }
-  const float l = __fmaf_rn(r.n[2 * E], ptx, __fmaf_rn(r.n[2 * E + 1], pty, r.c[E]));
+  const float l = __fmaf_rn(r.ed[E].nx, ptx, __fmaf_rn(r.ed[E].ny, pty, r.ed[E].c));
   live = live && !(l < -r.rej);
   const bool deep = l > r.acc;
   const SegEval g = seg_exact(r, E, ptx, pty);
