@@ -256,6 +256,32 @@ def fit_metric(dev, with_cpu: bool):
     return out
 
 
+def forward_metric(dev, P, sm_mhz: float, sms: int) -> dict:
+    """The headline cell's forward alone: `dr_render` into a (B, 3, H, W) image,
+    what `torch_layer.rasterize` runs (62 FP32 FLOP and 3 SFU operations per
+    bounding-box pair; the image written is 12 bytes per pixel)."""
+    import torch
+
+    from diffrast import _native
+    from diffrast import scenes as S
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ms = time_device(lambda: _native.render(P, H, W, SIGMA, layout=_native.LAYOUT_BCHW), 50, 5,
+                     flush, stream)
+    n_bbox = S.bbox_pairs(P.cpu().numpy(), H, W, SIGMA)
+    fp32, sfu = peaks_at(sm_mhz, sms)
+    img_bytes = P.shape[0] * 3 * H * W * 4
+    s = ms / 1e3
+    return {"metric": "forward-only render (dr_render, BCHW, the rasterize forward)",
+            "ms_per_step": ms, "dense_pair_evals_per_s": P.shape[0] * P.shape[1] * H * W / s,
+            "bbox_pair_evals_per_s": n_bbox / s, "fp32_frac": n_bbox * 62 / s / fp32,
+            "sfu_frac": n_bbox * 3 / s / sfu, "image_bytes": img_bytes,
+            "image_write_gb_s": img_bytes / s / 1e9,
+            "timing": "CUDA events, median of 50 calls, L2 flushed before each; set-up and "
+                      "raster kernels"}
+
+
 def host_identity() -> dict:
     """CPU model and logical core count of the box the CPU baselines run on."""
     model = None
@@ -752,6 +778,8 @@ def main():
             line["config4_sharded"] = sharded4
         if not args.no_fit and world == 1:
             line["secondary"] = fit_metric(dev, not args.no_cpu_baseline)
+        if not args.no_configs and world == 1:
+            line["forward"] = forward_metric(dev, P, sm_mhz, sms)
         if not args.no_configs and world == 1:
             line["configs"] = run_configs(dev, sm_mhz, not args.no_cpu_baseline)
         if not args.no_cpu_baseline and world == 1:

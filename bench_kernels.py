@@ -74,13 +74,15 @@ def main(argv=None) -> None:
     ap.add_argument("--fit-iters", type=int, default=0)
     ap.add_argument("--config", choices=("4", "5", "2-512", "2-128"))
     ap.add_argument("--batch", type=int, default=32, help="scenes of config 2-128")
+    ap.add_argument("--forward", action="store_true",
+                    help="with --config: time the forward alone (dr_render, BCHW)")
     ap.add_argument("--steps", type=int, default=3)
     args = ap.parse_args(argv)
     if args.fit_iters > 0:
         fit_graph(args.fit_iters)
         return
     if args.config:
-        config_steps(args.config, args.steps, args.batch)
+        config_steps(args.config, args.steps, args.batch, args.forward)
         return
     peak, src = _peak_gbs()
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -118,7 +120,7 @@ def main(argv=None) -> None:
     line("dr_adam_kernel", 28 * npar, ms, f"{npar} parameters")
 
 
-def config_steps(config: str, steps: int, batch: int = 32) -> None:
+def config_steps(config: str, steps: int, batch: int = 32, forward: bool = False) -> None:
     from diffrast import scenes as S
 
     if config == "4":
@@ -133,9 +135,13 @@ def config_steps(config: str, steps: int, batch: int = 32) -> None:
     P = torch.from_numpy(p).cuda()
     target = _native.render(torch.from_numpy(tp).cuda(), size, size, 0.0015)
     path = _native.query_path(P.shape[0], P.shape[1], size, size)
-    ms = [_time(lambda: _native.loss_backward(P, target, 0.0015), 1) for _ in range(steps)]
+    if forward:
+        call = lambda: _native.render(P, size, size, 0.0015, layout=_native.LAYOUT_BCHW)  # noqa: E731
+    else:
+        call = lambda: _native.loss_backward(P, target, 0.0015)  # noqa: E731
+    ms = [_time(call, 1) for _ in range(steps)]
     print(json.dumps({"config": config, "B": P.shape[0], "T": P.shape[1], "size": size,
-                      "path": path, "ms_per_call": ms}), flush=True)
+                      "path": path, "forward": forward, "ms_per_call": ms}), flush=True)
 
 
 def fit_graph(iters: int) -> None:

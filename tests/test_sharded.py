@@ -414,7 +414,7 @@ def _leaving_worker(rank, world, port, out):
 
 
 def test_a_departed_peer_ends_the_next_step_with_an_error():
-    # SURVEY's failure detection on the host: a rank that leaves between steps
+    # Failure detection on the host: a rank that leaves between steps
     # (no kernel or collective of its own in flight) must make the others'
     # next collective fail within the process group's timeout, not hang.
     ctx = mp.get_context("spawn")

@@ -5,7 +5,7 @@ The rasterizer itself needs a GPU; here a CPU stand-in with the same contract
 takes its place, so these tests check only the scaling and the DDP wiring:
 - global_fused_mse: each rank's gradient on its own scenes equals the gradient
   of the single-process mean over all B_global scenes (python/train.py:127-179
-  under DDP, SURVEY's config 3 sharded over ranks);
+  under DDP, the benchmark's config 3 sharded over ranks);
 - train_step under DistributedDataParallel: the averaged model gradient equals
   the single-process gradient on the whole batch.
 """
