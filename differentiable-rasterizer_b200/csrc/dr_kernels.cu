@@ -292,6 +292,29 @@ __device__ __forceinline__ int classify_block(const TriRec& r, int bx0, int by0,
       if (!(__fsub_rn(fabsf(lc), rad) > thr)) cand |= 1 << e;
     }
     if (lmin_all > r.acc) return kBlkInside;  // deep inside implies inside the box
+    if ((cand & (cand - 1)) && lmin_all > r.margin) {
+      // Two or three candidates, every pixel inside every edge line. There the
+      // nearest segment is the nearest line (the largest disk around the
+      // pixel inside the triangle touches its nearest line within the
+      // segment), so an edge whose line lies farther from every pixel than
+      // some other edge's line lies from any pixel is never the nearest, not
+      // even within rounding: drop it (its cross product has the winding's
+      // sign, as for any non-candidate). Near one edge and deep from the
+      // others, the block becomes single-edge.
+      float lmin[3], umin = __int_as_float(0x7f800000);
+#pragma unroll
+      for (int e = 0; e < 3; ++e) {
+        const float nx = r.ed[e].nx, ny = r.ed[e].ny;
+        const float lc = __fmaf_rn(nx, cx, __fmaf_rn(ny, cy, r.ed[e].c));
+        const float rad = __fmaf_rn(fabsf(nx), hx, __fmul_rn(fabsf(ny), hy));
+        lmin[e] = __fsub_rn(lc, rad);
+        umin = fminf(umin, __fadd_rn(lc, rad));
+      }
+      const float lim = __fadd_rn(umin, __fmul_rn(2.0f, r.margin));
+#pragma unroll
+      for (int e = 0; e < 3; ++e)
+        if (lmin[e] > lim) cand &= ~(1 << e);
+    }
     code |= cand << kCandShift;
   } else {
     code |= 7 << kCandShift;
