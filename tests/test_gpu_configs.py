@@ -119,6 +119,28 @@ def test_config2_cells_full_batch(native, oracle, T, size):
     full_parity(native, oracle, p, target, 0.0015, name=f"config2_T{T}_{size}")
 
 
+@pytest.mark.parametrize("T", [128, 512])
+def test_config2_wide_band_cells(native, oracle, T):
+    # Config 2's second sigma (0.01): bands wide against an 8x4 block, where
+    # the classification prunes candidate edges with its corner bounds.
+    from diffrast.scenes import config2_params
+
+    cell = [32, 128, 512].index(T) * 3 + 2
+    p, tp = config2_params(32, T, cell)
+    target = oracle.render_batch(tp, 256, 256, 0.01)
+    full_parity(native, oracle, p, target, 0.01, name=f"config2_T{T}_256_s0.01")
+
+
+def test_config4_full_scene(native, oracle):
+    # Config 4: one 1024^2 scene of 4096 small triangles (gathered tile lists).
+    from diffrast.scenes import config4_params
+
+    p = config4_params(4096, 4000)
+    assert native.query_path(1, 4096, 1024, 1024) == native.PATH_TILE_GATHER
+    target = oracle.render_batch(config4_params(4096, 4001), 1024, 1024, 0.0015)
+    full_parity(native, oracle, p, target, 0.0015, name="config4")
+
+
 @pytest.mark.parametrize("sigma", [0.00015, 0.0015, 0.015])
 def test_config5_full_batch(native, oracle, sigma):
     # All 16 seeded stress scenes (seeds 5000..5015): heavy overlap, 5 %
