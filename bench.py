@@ -552,9 +552,10 @@ def run_reference(args, rank: int, world: int):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded PCG64 scenes, config 2 distribution)",
         "config": {"workload": "config2 B=32 T=128 256x256 sigma=0.0015 fwd+mse+bwd",
+                   "entry": "oracle (C++ restatement of the Rust CPU path)",
                    "global_batch": B, "seq_len": None, "parallelism": "cpu threads"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{n} of the {B} scenes per step (a full step takes "
@@ -742,8 +743,8 @@ def main():
             "higher_is_better": True, "scaling": "strong" if strong or world == 1 else "weak",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded PCG64 scenes, config 2 distribution)",
-            "config": {"workload": "config2 B=32 T=128 256x256 sigma=0.0015 fwd+mse+bwd "
-                                   "(dr_loss_backward)",
+            "config": {"workload": "config2 B=32 T=128 256x256 sigma=0.0015 fwd+mse+bwd",
+                       "entry": "dr_loss_backward",
                        "global_batch": global_scenes, "seq_len": None,
                        "parallelism": (f"batch-sharded x{world}: {n_local} scenes per GPU, "
                                        "no collective"),

@@ -172,6 +172,17 @@ extern "C" {
     pub fn dr_set_reduce_mode(ctx: *mut dr_ctx, mode: c_int) -> dr_status;
     pub fn dr_get_reduce_mode(ctx: *mut dr_ctx, mode: *mut c_int) -> dr_status;
     pub fn dr_set_deterministic(ctx: *mut dr_ctx, on: c_int) -> dr_status;
+    pub fn dr_pixel_tape_bytes(b: c_int, height: c_int, width: c_int) -> u64;
+    pub fn dr_render_taped(ctx: *mut dr_ctx, params: *const c_float, background: *const c_float,
+                           bg_per_scene: c_int, b: c_int, t: c_int, height: c_int, width: c_int,
+                           sigma: c_float, layout: c_int, image: *mut c_float, tape: *mut c_void,
+                           stream: dr_stream_t) -> dr_status;
+    pub fn dr_grad_backward_taped(ctx: *mut dr_ctx, params: *const c_float,
+                                  background: *const c_float, bg_per_scene: c_int, b: c_int,
+                                  t: c_int, height: c_int, width: c_int, sigma: c_float,
+                                  grad_images: *const c_float, layout: c_int,
+                                  tape: *const c_void, grads: *mut c_float,
+                                  stream: dr_stream_t) -> dr_status;
     pub fn dr_get_deterministic(ctx: *mut dr_ctx, on: *mut c_int) -> dr_status;
     pub fn dr_loss_backward_timed(ctx: *mut dr_ctx, params: *const c_float,
                                   background: *const c_float, bg_per_scene: c_int, b: c_int,

@@ -268,10 +268,19 @@ dr_status det_scratch(dr_ctx* ctx, RasterArgs& a, size_t n_tris, cudaStream_t s)
   return DR_OK;
 }
 
+// Bytes of the pixel tape's flag header (one int per scene and region,
+// rounded up to 16 bytes) and of the whole tape.
+size_t tape_header_bytes(int B, int H, int W) {
+  const int tiles_x = (W + kTileSide - 1) / kTileSide, tiles_y = (H + kTileSide - 1) / kTileSide;
+  const size_t n = (size_t)B * tape_regions(tiles_x, tiles_y) * sizeof(int);
+  return (n + 15) / 16 * 16;
+}
+
 dr_status backward_common(dr_ctx* ctx, int mode, const float* params, const float* background,
                           int bg_per_scene, int B, int T, int H, int W, float sigma,
                           const float* other, int layout, int shard, int n_shards, float* grads,
-                          float* losses, double* loss_sums, float* image, cudaStream_t s) {
+                          float* losses, double* loss_sums, float* image, cudaStream_t s,
+                          const void* tape = nullptr) {
   dr_status st = check_common(ctx, params, B, T, H, W, sigma, layout);
   if (st) return st;
   if (B > 0 && (!other || (T > 0 && !grads)))
@@ -296,6 +305,10 @@ dr_status backward_common(dr_ctx* ctx, int mode, const float* params, const floa
   a.image = image;
   a.losses = losses;
   a.loss_sums = loss_sums;
+  if (tape && n_shards == 1) {
+    a.tape_flags = (int*)tape;
+    a.tape = (float4*)((unsigned char*)tape + tape_header_bytes(B, H, W));
+  }
   if (mode == kModeLoss) {
     if (n_tiles == 0) {
       if (losses) DR_CUDA(cudaMemsetAsync(losses, 0, sizeof(float) * B, s), "zero losses");
@@ -479,6 +492,49 @@ dr_status dr_grad_backward(dr_ctx* ctx, const float* params, const float* backgr
   return backward_common(ctx, kModeGrad, params, background, bg_per_scene, B, T, H, W, sigma,
                          grad_images, layout, 0, 1, grads, nullptr, nullptr, nullptr,
                          (cudaStream_t)stream);
+}
+
+uint64_t dr_pixel_tape_bytes(int B, int H, int W) {
+  if (B < 0 || H <= 0 || W <= 0) return 0;
+  return tape_header_bytes(B, H, W) + (uint64_t)B * H * W * sizeof(float4);
+}
+
+dr_status dr_render_taped(dr_ctx* ctx, const float* params, const float* background,
+                          int bg_per_scene, int B, int T, int H, int W, float sigma, int layout,
+                          float* image, void* tape, dr_stream_t stream) {
+  dr_status st = check_common(ctx, params, B, T, H, W, sigma, layout);
+  if (st) return st;
+  if (B > 0 && (!image || !tape)) return fail(DR_INVALID_ARGUMENT, "null image or tape pointer");
+  if (((uintptr_t)tape & 15u) != 0) return fail(DR_INVALID_ARGUMENT, "tape must be 16-byte aligned");
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  DeviceGuard g(ctx->device);
+  if (B == 0) return DR_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  RasterArgs a;
+  st = prepare(ctx, params, background, bg_per_scene, B, T, H, W, sigma, layout, 0, a, s);
+  if (st) return st;
+  a.image = image;
+  const int tiles_y = (H + kTileSide - 1) / kTileSide;
+  const int n_tiles = a.tiles_x * tiles_y;
+  if (raster_path(B, T, a.tiles_x, tiles_y, 1) == 1) {
+    a.tape_flags = (int*)tape;
+    a.tape = (float4*)((unsigned char*)tape + tape_header_bytes(B, H, W));
+  } else {  // only the region kernel keeps a tape: flag every region
+    DR_CUDA(cudaMemsetAsync(tape, 1, tape_header_bytes(B, H, W), s), "flag the tape unused");
+  }
+  DR_CUDA(launch_raster(kModeRender, a, n_tiles, s), "raster kernel");
+  return DR_OK;
+}
+
+dr_status dr_grad_backward_taped(dr_ctx* ctx, const float* params, const float* background,
+                                 int bg_per_scene, int B, int T, int H, int W, float sigma,
+                                 const float* grad_images, int layout, const void* tape,
+                                 float* grads, dr_stream_t stream) {
+  if (B > 0 && !tape) return fail(DR_INVALID_ARGUMENT, "null tape pointer");
+  if (((uintptr_t)tape & 15u) != 0) return fail(DR_INVALID_ARGUMENT, "tape must be 16-byte aligned");
+  return backward_common(ctx, kModeGrad, params, background, bg_per_scene, B, T, H, W, sigma,
+                         grad_images, layout, 0, 1, grads, nullptr, nullptr, nullptr,
+                         (cudaStream_t)stream, tape);
 }
 
 dr_status dr_loss_backward_sharded(dr_ctx* ctx, const float* params, const float* background,

@@ -51,6 +51,11 @@ struct RasterArgs {
   // zero on entry; launch_det_finalize turns them into `grads`.
   long long* grads_fx;
   int* grads_nf;
+  // Pixel tape (dr_render_taped / dr_grad_backward_taped), else null: per pixel
+  // of the batch the forward's running product (m, e, z0, zn), and per (scene,
+  // region) a flag, nonzero where the tape cannot stand in for the forward.
+  float4* tape;
+  int* tape_flags;
   // dr_fit only (B = 1): the CTA that completes the loss also runs Fitter::step's
   // bookkeeping for iteration fit_iter (fit.rs:243-288).
   FitState* fit;
@@ -106,6 +111,8 @@ cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream
 // non-finite flags nf[i / 10], n = B * T * 10 values; fx and nf are left zero
 // for the next launch.
 cudaError_t launch_det_finalize(long long* fx, int* nf, float* grads, long long n, cudaStream_t s);
+// Regions per scene of the region kernel (the pixel tape's flags per scene).
+long long tape_regions(int tiles_x, int tile_rows);
 // Which kernel a launch over B scenes of tiles_x x tile_rows tiles takes:
 // 0 the tile kernel, 1 the region kernel, 2 the triangle-block split (split_k > 1).
 int raster_path(int B, int T, int tiles_x, int tile_rows, int split_k);

@@ -1085,7 +1085,7 @@ __device__ __forceinline__ void acc_add(S& sm, int j, int p, float v, bool det) 
 // Pass 1 over a staged list for one lane's pixel: composites in order
 // (raster.rs:63) and keeps the running product of 1 - w. `col` selects the
 // warp's block code.
-template <int Mode, int kPrec, class S>
+template <int Mode, int kPrec, class S, bool kProd = Mode != kModeRender>
 __device__ __forceinline__ void forward_walk(const S& sm, int count, int col, int px, int py,
                                              float ptx, float pty, bool active, const Consts& K,
                                              float& c0, float& c1, float& c2, Prod& P) {
@@ -1114,7 +1114,7 @@ __device__ __forceinline__ void forward_walk(const S& sm, int count, int col, in
     c0 = __fadd_rn(__fmul_rn(r.color[0], w), __fmul_rn(c0, om));  // raster.rs:63
     c1 = __fadd_rn(__fmul_rn(r.color[1], w), __fmul_rn(c1, om));
     c2 = __fadd_rn(__fmul_rn(r.color[2], w), __fmul_rn(c2, om));
-    if (Mode != kModeRender) P.mul(om, k);
+    if (kProd) P.mul(om, k);
   }
 }
 
@@ -1631,7 +1631,11 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
 // region's warp blocks, warps taking blocks from a shared counter. A warp that
 // finishes a cheap block takes the next one instead of waiting for the CTA's
 // busiest warp; there is no barrier between the list and the final flush.
-template <int Mode, int kPrec, int kRows, bool kDet = false>
+// kTape: 0 none; 1 (render) also writes each pixel's running product to the
+// pixel tape, and per region whether the tape stands in for the forward; 2
+// (grad) reads the products back instead of running the forward walk, in
+// regions whose flag allows it.
+template <int Mode, int kPrec, int kRows, bool kDet = false, int kTape = 0>
 __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArgs a) {
   constexpr int kRB = kRegionCols * kRows * kBlocksPerTile;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1659,6 +1663,18 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArg
 
   if (threadIdx.x == 0) sm.next_block = kWarps;
   const int count = build_region_list(sm, a, a.recs + (size_t)b * a.T, rx0, lrow0);
+  const size_t flag_at = (size_t)b * n_regions + region;
+  if (kTape == 1) {
+    // The forward keeps render()'s semantics (a NaN-alpha triangle paints
+    // NaN, raster.rs:49); the backward drops such a triangle (grad.rs:62). A
+    // region that holds one has a different running product there: flag it.
+    int nan_alpha = 0;
+    for (int j = threadIdx.x; j < count; j += kThreads) nan_alpha |= sm.rec[j].alpha != sm.rec[j].alpha;
+    nan_alpha = __syncthreads_or(nan_alpha);
+    if (threadIdx.x == 0) a.tape_flags[flag_at] = nan_alpha;
+  }
+  bool from_tape = false;
+  if (kTape == 2) from_tape = a.tape_flags[flag_at] == 0 && a.image == nullptr;
 
   // Blocks are taken at most once each, so no warp runs more than kRB
   // iterations.
@@ -1673,7 +1689,21 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_region_kernel(RasterArg
     scene_background(a, b, c0, c1, c2);
     Prod P;
     P.init();
-    forward_walk<Mode, kPrec>(sm, count, blk, px, py, ptx, pty, active, K, c0, c1, c2, P);
+    const size_t pix = ((size_t)b * a.H + py) * a.W + px;
+    if (kTape == 2 && from_tape) {
+      if (active) {
+        const float4 t = a.tape[pix];
+        P.m = t.x;
+        P.e = __float_as_int(t.y);
+        P.z0 = __float_as_int(t.z);
+        P.zn = __float_as_int(t.w);
+      }
+    } else {
+      forward_walk<Mode, kPrec, RegionSmem<kRB>, Mode != kModeRender || kTape == 1>(
+          sm, count, blk, px, py, ptx, pty, active, K, c0, c1, c2, P);
+    }
+    if (kTape == 1 && active)
+      a.tape[pix] = make_float4(P.m, __int_as_float(P.e), __int_as_float(P.z0), __int_as_float(P.zn));
     if (a.image) store_block(a, b, x0, y0, lane, c0, c1, c2, sm.stage[warp]);
     if (Mode != kModeRender) {
       float G0, G1, G2;
@@ -1963,6 +1993,18 @@ static cudaError_t launch_mode(const RasterArgs& a, int n_tiles, cudaStream_t s)
   if (use_region_kernel(a.B, a.T, a.tiles_x, a.tile_rows)) {
     if (n_ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     const unsigned grid = (unsigned)n_ctas;
+    if constexpr (Mode == kModeRender || Mode == kModeGrad) {
+      if (a.tape) {  // the pixel tape: written by a render, read by a grad call
+        constexpr int kTape = Mode == kModeRender ? 1 : 2;
+        if (det)
+          dr_raster_region_kernel<Mode, kPrec, kRows, kGrads, kTape>
+              <<<grid, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);
+        else
+          dr_raster_region_kernel<Mode, kPrec, kRows, false, kTape>
+              <<<grid, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);
+        return cudaGetLastError();
+      }
+    }
     if (det)
       dr_raster_region_kernel<Mode, kPrec, kRows, kGrads>
           <<<grid, kThreads, sizeof(RegionSmem<kRB>), s>>>(a);
@@ -2115,6 +2157,13 @@ cudaError_t launch_det_finalize(long long* fx, int* nf, float* grads, long long 
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   dr_det_finalize_kernel<<<(unsigned)blocks, 256, 0, s>>>(fx, nf, grads, n_tris);
   return cudaGetLastError();
+}
+
+// Per (scene, region) flags of the pixel tape for a launch over B scenes of
+// tiles_x x tile_rows tiles: how many regions the region kernel uses.
+long long tape_regions(int tiles_x, int tile_rows) {
+  return (long long)((tiles_x + kRegionCols - 1) / kRegionCols) *
+         ((tile_rows + kRegionRows - 1) / kRegionRows);
 }
 
 cudaError_t launch_raster(int mode, const RasterArgs& args, int n_tiles, cudaStream_t s) {

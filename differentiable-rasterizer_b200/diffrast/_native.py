@@ -112,6 +112,9 @@ SIGNATURES = {
     "dr_set_reduce_mode": (_I, [_P, _I]),
     "dr_get_reduce_mode": (_I, [_P, ctypes.POINTER(_I)]),
     "dr_set_deterministic": (_I, [_P, _I]),
+    "dr_pixel_tape_bytes": (ctypes.c_uint64, [_I, _I, _I]),
+    "dr_render_taped": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P, _P, _P]),
+    "dr_grad_backward_taped": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P, _P]),
     "dr_get_deterministic": (_I, [_P, ctypes.POINTER(_I)]),
     "dr_loss_backward_timed": (
         _I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P,
@@ -367,6 +370,55 @@ def render(params: torch.Tensor, height: int, width: int, sigma: float, backgrou
     check(lib().dr_render(context(dev, s), _ptr(p), _ptr(bg), per, B, T, height, width, sigma,
                           layout, _ptr(out), ctypes.c_void_p(s)))
     return out
+
+
+def pixel_tape_bytes(B: int, height: int, width: int) -> int:
+    """dr_pixel_tape_bytes: the compact forward tape's size."""
+    return int(lib().dr_pixel_tape_bytes(B, height, width))
+
+
+def render_taped(params: torch.Tensor, height: int, width: int, sigma: float,
+                 background=(0.0, 0.0, 0.0), layout: int = LAYOUT_BHWC,
+                 device: torch.device | None = None):
+    """dr_render_taped: the image as `render` returns it, and the pixel tape
+    (a uint8 device tensor) that `grad_backward_taped` reads back."""
+    sigma = _check_sigma(sigma)
+    dev = _resolve_device(device if device is not None else params.device)
+    p = _as_cuda_f32(params, dev)
+    B, T = p.shape[0], p.shape[1]
+    shape = (B, 3, height, width) if layout == LAYOUT_BCHW else (B, height, width, 3)
+    out = torch.empty(shape, dtype=torch.float32, device=dev)
+    tape = torch.empty(pixel_tape_bytes(B, height, width), dtype=torch.uint8, device=dev)
+    bg, per = _bg_host(background, B)
+    s = _stream(dev)
+    check(lib().dr_render_taped(context(dev, s), _ptr(p), _ptr(bg), per, B, T, height, width,
+                                sigma, layout, _ptr(out), _ptr(tape), ctypes.c_void_p(s)))
+    return out, tape
+
+
+def grad_backward_taped(params: torch.Tensor, grad_images: torch.Tensor, tape: torch.Tensor,
+                        sigma: float, background=(0.0, 0.0, 0.0), layout: int = LAYOUT_BHWC,
+                        device: torch.device | None = None) -> torch.Tensor:
+    """dr_grad_backward_taped: `grad_backward` with the forward read from the
+    tape of `render_taped` (same params, sizes, sigma and background)."""
+    sigma = _check_sigma(sigma)
+    dev = _resolve_device(device if device is not None else params.device)
+    p = _as_cuda_f32(params, dev)
+    g = _as_cuda_f32(grad_images, dev)
+    B, T = p.shape[0], p.shape[1]
+    if layout == LAYOUT_BCHW:
+        H, W = g.shape[2], g.shape[3]
+    else:
+        H, W = g.shape[1], g.shape[2]
+    if tape.device != dev or tape.numel() < pixel_tape_bytes(B, H, W):
+        raise ValueError("tape does not belong to a render of this batch on this device")
+    grads = torch.empty((B, T, N_PARAMS), dtype=torch.float32, device=dev)
+    bg, per = _bg_host(background, B)
+    s = _stream(dev)
+    check(lib().dr_grad_backward_taped(context(dev, s), _ptr(p), _ptr(bg), per, B, T, H, W,
+                                       sigma, _ptr(g), layout, _ptr(tape), _ptr(grads),
+                                       ctypes.c_void_p(s)))
+    return grads
 
 
 HOST_CHUNKS_MAX = 5  # DR_HOST_CHUNKS_MAX

@@ -60,16 +60,34 @@ def _check_sigma(sigma: float) -> None:
         raise ValueError("sigma must be positive")
 
 
+# Largest pixel tape (16 bytes per pixel of the batch) the forward keeps for
+# the backward; larger batches recompute the forward in the backward.
+_TAPE_LIMIT = 1 << 29
+
+
 class _Rasterize(torch.autograd.Function):
-    """Forward = dr_render; backward = dr_grad_backward on the upstream gradient."""
+    """Forward = dr_render_taped (the image, plus each pixel's running product
+    of 1 - w); backward = dr_grad_backward_taped on the upstream gradient,
+    which reads the products back instead of running the forward walk again
+    (BackwardMode::Taped, compact). Calls that need no parameter gradient, and
+    batches whose tape would exceed _TAPE_LIMIT, take dr_render /
+    dr_grad_backward."""
 
     @staticmethod
     def forward(ctx, params: Tensor, height: int, width: int, sigma: float, background,
                 channels_first: bool):
         layout = _native.LAYOUT_BCHW if channels_first else _native.LAYOUT_BHWC
-        images = _native.render(params, height, width, sigma, background, layout)
+        B = params.shape[0]
+        tape = None
+        if ctx.needs_input_grad[0] and _native.pixel_tape_bytes(B, height, width) <= _TAPE_LIMIT:
+            images, tape = _native.render_taped(params, height, width, sigma, background, layout)
+        else:
+            images = _native.render(params, height, width, sigma, background, layout)
         _note_gpu()
-        ctx.save_for_backward(params)
+        if tape is None:
+            ctx.save_for_backward(params)
+        else:
+            ctx.save_for_backward(params, tape)
         ctx.sigma = sigma
         ctx.background = background
         ctx.layout = layout
@@ -77,8 +95,14 @@ class _Rasterize(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_images: Tensor):
-        (params,) = ctx.saved_tensors
-        grads = _native.grad_backward(params, grad_images, ctx.sigma, ctx.background, ctx.layout)
+        saved = ctx.saved_tensors
+        params = saved[0]
+        if len(saved) == 2:
+            grads = _native.grad_backward_taped(params, grad_images, saved[1], ctx.sigma,
+                                                ctx.background, ctx.layout)
+        else:
+            grads = _native.grad_backward(params, grad_images, ctx.sigma, ctx.background,
+                                          ctx.layout)
         _note_gpu()
         grad_params = grads.to(params.device, params.dtype)
         return grad_params, None, None, None, None, None

@@ -197,6 +197,30 @@ DR_API dr_status dr_grad_backward(dr_ctx* ctx, const float* params, const float*
                            const float* grad_images, int layout, float* grads,
                            dr_stream_t stream);
 
+/* The taped pair of render_with_tape + backward_from_grad (grad.rs:56-106;
+ * BackwardMode::Taped, diffrast-gpu/src/lib.rs:211-220) in a compact form:
+ * instead of every triangle's coverage (T x H x W x 12 bytes, tape_bytes),
+ * the tape holds one 16-byte word per pixel, the forward's running product of
+ * (1 - w) (mantissa, exponent and its last zero and NaN layers), plus a flag
+ * word per (scene, 32x16 region). dr_render_taped renders exactly as
+ * dr_render and fills the tape; dr_grad_backward_taped, given the same
+ * params, sizes, sigma and background, returns exactly what dr_grad_backward
+ * returns, reading the products back instead of running the forward walk
+ * again. Where the tape cannot stand in (a region holding a NaN-alpha
+ * triangle, which render() paints and the backward drops; shapes that do not
+ * take the region kernel) the backward recomputes. The
+ * tape is caller-owned device memory of dr_pixel_tape_bytes(B, H, W) bytes,
+ * 16-byte aligned. No reference counterpart for the compact form. */
+DR_API uint64_t dr_pixel_tape_bytes(int B, int H, int W);
+DR_API dr_status dr_render_taped(dr_ctx* ctx, const float* params, const float* background,
+                                 int bg_per_scene, int B, int T, int H, int W, float sigma,
+                                 int layout, float* image, void* tape, dr_stream_t stream);
+DR_API dr_status dr_grad_backward_taped(dr_ctx* ctx, const float* params,
+                                        const float* background, int bg_per_scene, int B, int T,
+                                        int H, int W, float sigma, const float* grad_images,
+                                        int layout, const void* tape, float* grads,
+                                        dr_stream_t stream);
+
 /* Row-sharded dr_loss_backward for one large scene split across devices: this
  * call covers the 16-pixel tile rows r with r % n_shards == shard. grads
  * receives this shard's partial gradient (overwritten); loss_sums (B,) f64
