@@ -131,6 +131,35 @@ def test_config2_wide_band_cells(native, oracle, T):
     full_parity(native, oracle, p, target, 0.01, name=f"config2_T{T}_256_s0.01")
 
 
+def test_config3_torch_op_full_batch(native, oracle):
+    # Config 3 exactly as the bench times it: activate(raw) params for 256
+    # scenes of 64 triangles, targets rendered from random_params, then
+    # rasterize -> F.mse_loss -> backward (the forward keeps the pixel tape).
+    import torch.nn.functional as F
+
+    from diffrast import torch_layer
+
+    raw = torch.randn(256, 64, 10, generator=torch.Generator().manual_seed(2))
+    params = torch_layer.activate(raw)
+    tparams = torch_layer.random_params(256, 64, generator=torch.Generator().manual_seed(3))
+    targets = torch_layer.rasterize(tparams.cuda(), 128, 128, 0.0015).detach()
+    q = params.cuda().requires_grad_(True)
+    img = torch_layer.rasterize(q, 128, 128, 0.0015)
+    loss = F.mse_loss(img, targets)
+    loss.backward()
+    p_np = params.numpy()
+    t_hwc = targets.permute(0, 2, 3, 1).contiguous().cpu().numpy()
+    ref_l, ref_g, ref_img = oracle.backward_batch(p_np, t_hwc, 0.0015, want_images=True)
+    assert_images_close(host(img).transpose(0, 2, 3, 1), ref_img, "config 3 render")
+    np.testing.assert_allclose(float(loss), float(np.mean(ref_l)), rtol=1e-5)
+    # F.mse_loss averages over the whole batch: the per-scene gradients / B.
+    assert_grads_close(host(q.grad), ref_g / 256, "config 3 grads")
+    report("config3", image_max_abs=float(np.nanmax(np.abs(host(img).transpose(0, 2, 3, 1) -
+                                                           ref_img))),
+           grad_max_excess=max_excess(host(q.grad), ref_g / 256),
+           path=native.query_path(256, 64, 128, 128))
+
+
 def test_config4_full_scene(native, oracle):
     # Config 4: one 1024^2 scene of 4096 small triangles (gathered tile lists).
     from diffrast.scenes import config4_params
