@@ -233,11 +233,15 @@ dr_status prepare(dr_ctx* ctx, const float* params, const float* background, int
             "copy backgrounds");
     a.bg_dev = (const float*)ctx->bgbuf.ptr;
   }
+  // The records, then their pixel boxes packed (the tile masks read these).
   size_t rec_bytes = tri_rec_bytes() * (size_t)B * (size_t)T;
-  dr_status st = ensure(ctx, ctx->recs, rec_bytes, false);
+  dr_status st = ensure(ctx, ctx->recs, rec_bytes + sizeof(int4) * (size_t)B * T, false);
   if (st) return st;
   a.recs = (const TriRec*)ctx->recs.ptr;
-  DR_CUDA(launch_setup(params, B * T, W, H, sigma, tape, (TriRec*)ctx->recs.ptr, s), "set-up kernel");
+  int4* boxes = (int4*)((unsigned char*)ctx->recs.ptr + rec_bytes);
+  a.boxes = boxes;
+  DR_CUDA(launch_setup(params, B * T, W, H, sigma, tape, (TriRec*)ctx->recs.ptr, s, boxes),
+          "set-up kernel");
   return DR_OK;
 }
 
@@ -647,7 +651,8 @@ dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params, const float* b
   if ((st = ensure(ctx, ctx->io_targets, sizeof(float) * per_t * B, false))) return st;
   if ((st = ensure(ctx, ctx->io_grads, sizeof(float) * per_p * B, false))) return st;
   if ((st = ensure(ctx, ctx->io_losses, sizeof(float) * (size_t)B, false))) return st;
-  if ((st = ensure(ctx, ctx->recs, tri_rec_bytes() * (size_t)B * T, false))) return st;
+  if ((st = ensure(ctx, ctx->recs, (tri_rec_bytes() + sizeof(int4)) * (size_t)B * T, false)))
+    return st;
   if ((st = ensure(ctx, ctx->partials, sizeof(double) * (size_t)B * tiles, false))) return st;
   if ((st = ensure(ctx, ctx->counters, sizeof(unsigned) * (size_t)B, true))) return st;
   if (split_at[nc] && (st = ensure(ctx, ctx->split, split_at[nc], false))) return st;
@@ -733,7 +738,10 @@ dr_status dr_loss_backward_host(dr_ctx* ctx, const float* params, const float* b
       a.bg3[2] = background[2];
     }
     a.recs = R + l * T;
-    chk(launch_setup(P + l * per_p, n * T, W, H, sigma, 1, R + l * T, q), "set-up kernel");
+    int4* boxes = (int4*)(R + (size_t)B * T) + l * T;  // packed boxes after all records
+    a.boxes = boxes;
+    chk(launch_setup(P + l * per_p, n * T, W, H, sigma, 1, R + l * T, q, boxes),
+        "set-up kernel");
     a.other = Tg + l * per_t;
     a.grads = G + l * per_p;
     a.losses = L + l;
@@ -843,7 +851,8 @@ dr_status dr_loss_backward_timed(dr_ctx* ctx, const float* params, const float* 
   if ((st = ensure(ctx, ctx->io_targets, sizeof(float) * nt, false))) return st;
   if ((st = ensure(ctx, ctx->io_grads, sizeof(float) * np, false))) return st;
   if ((st = ensure(ctx, ctx->io_losses, sizeof(float) * (size_t)B, false))) return st;
-  if ((st = ensure(ctx, ctx->recs, tri_rec_bytes() * (size_t)B * T, false))) return st;
+  if ((st = ensure(ctx, ctx->recs, (tri_rec_bytes() + sizeof(int4)) * (size_t)B * T, false)))
+    return st;
   if ((st = ensure(ctx, ctx->partials, sizeof(double) * (size_t)B * tiles, false))) return st;
   if ((st = ensure(ctx, ctx->counters, sizeof(unsigned) * (size_t)B, true))) return st;
   if (k > 1 && (st = ensure(ctx, ctx->split, raster_split_bytes(B, k, H, W), false))) return st;
@@ -893,7 +902,10 @@ dr_status dr_loss_backward_timed(dr_ctx* ctx, const float* params, const float* 
       a.bg3[2] = background[2];
     }
     a.recs = (const TriRec*)ctx->recs.ptr;
-    chk(launch_setup(P, B * T, W, H, sigma, 1, (TriRec*)ctx->recs.ptr, s), "set-up kernel");
+    int4* boxes = (int4*)((unsigned char*)ctx->recs.ptr + tri_rec_bytes() * (size_t)B * T);
+    a.boxes = boxes;
+    chk(launch_setup(P, B * T, W, H, sigma, 1, (TriRec*)ctx->recs.ptr, s, boxes),
+        "set-up kernel");
     chk(cudaEventRecord(ev[1], s), "recording an event");
     // dispatch: the fused kernel.
     if (T > 0) chk(cudaMemsetAsync(G, 0, sizeof(float) * np, s), "zeroing gradients");
@@ -953,7 +965,8 @@ uint64_t dr_scratch_bytes(dr_ctx* ctx, int B, int T, int H, int W) {
     DeviceGuard g(ctx->device);
     k = ctx->split_blocks ? ctx->split_blocks : raster_split_blocks(B, T, tiles);
   }
-  uint64_t b = (uint64_t)tri_rec_bytes() * B * T + sizeof(double) * (uint64_t)B * tiles +
+  uint64_t b = (uint64_t)(tri_rec_bytes() + sizeof(int4)) * B * T +
+               sizeof(double) * (uint64_t)B * tiles +
                sizeof(unsigned) * (uint64_t)B;
   if (k > 1) b += raster_split_bytes(B, k, H, W);
   return b;

@@ -22,6 +22,9 @@ struct FitState;
 
 struct RasterArgs {
   const TriRec* recs;  // B*T records from the set-up kernel
+  // Optional: the records' pixel boxes again, 16 bytes each, packed (empty
+  // for triangles that cannot paint): the tile masks read these.
+  const int4* boxes;
   int B, T, H, W;
   int tiles_x;
   int tile_row0, tile_row_step;  // tile rows covered: row0 + i * step
@@ -104,8 +107,10 @@ cudaError_t launch_fit_init(FitState* st, cudaStream_t s);
 cudaError_t launch_fit_adam_setup(const AdamArgs& a, float* grads, int T, int W, int H,
                                   float next_sigma, TriRec* recs, cudaStream_t s);
 size_t tri_rec_bytes();
+// boxes (optional): each record's pixel box again, packed, for the tile masks.
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
-                         int tape_semantics, TriRec* recs, cudaStream_t s);
+                         int tape_semantics, TriRec* recs, cudaStream_t s,
+                         int4* boxes = nullptr);
 cudaError_t launch_raster(int mode, const RasterArgs& a, int n_tiles, cudaStream_t s);
 // Deterministic gradient sums: grads[i] from the fixed-point sum fx[i] and the
 // non-finite flags nf[i / 10], n = B * T * 10 values; fx and nf are left zero

@@ -175,13 +175,14 @@ __device__ __forceinline__ TriRec make_record(const float* __restrict__ params, 
 constexpr int kSetupThreads = 128;
 __global__ void __launch_bounds__(kSetupThreads) dr_setup_kernel(
     const float* __restrict__ params, int BT, int W, int H, float sigma, int tape_semantics,
-    TriRec* __restrict__ recs) {
+    TriRec* __restrict__ recs, int4* __restrict__ boxes) {
   constexpr int kQ = kRecWords / 4;  // float4s per record
   __shared__ float4 stage[kSetupThreads * kQ];
   const int first = blockIdx.x * kSetupThreads;
   const int i = first + (int)threadIdx.x;
   if (i < BT) {
     const TriRec r = make_record(params, i, W, H, sigma, tape_semantics);
+    if (boxes) boxes[i] = make_int4(r.bbox[0], r.bbox[1], r.bbox[2], r.bbox[3]);
     const float4* src = reinterpret_cast<const float4*>(&r);
 #pragma unroll
     for (int j = 0; j < kQ; ++j) stage[threadIdx.x * kQ + j] = src[j];
@@ -387,6 +388,7 @@ __device__ __forceinline__ int build_list(Smem& sm, const TriRec* __restrict__ r
 struct Range {
   int t0, t1;    // triangles [t0, t1) of the scene, at most kGatherMaxT
   int tx0, ty0;  // the tile's first pixel
+  const int4* boxes;  // the scene's packed pixel boxes, or null: the records' own
   __device__ int words() const { return (t1 - t0 + 31) / 32; }
 };
 
@@ -412,7 +414,7 @@ __device__ void tile_mask(Smem& sm, const TriRec* __restrict__ recs, const Range
       const int k = rg.t0 + 32 * j + lane;
       hit[u] = false;
       if (j < end && k < rg.t1) {
-        const int4 bb = *reinterpret_cast<const int4*>(recs[k].bbox);
+        const int4 bb = rg.boxes ? rg.boxes[k] : *reinterpret_cast<const int4*>(recs[k].bbox);
         hit[u] = bb.x < tx1 && bb.z > rg.tx0 && bb.y < ty1 && bb.w > rg.ty0;
       }
     }
@@ -1501,6 +1503,7 @@ __global__ void __launch_bounds__(kThreads, 4) dr_raster_kernel(RasterArgs a) {
   rg.t1 = t1;
   rg.tx0 = tx0;
   rg.ty0 = ty0;
+  rg.boxes = a.boxes ? a.boxes + (size_t)b * a.T : nullptr;
   if constexpr (kGather) n_chunks = (gather_start(sm, recs, rg, a.W, a.H) + kChunk - 1) / kChunk;
   Prod P;
   P.init();
@@ -1928,10 +1931,11 @@ cudaError_t launch_fit_adam_setup(const AdamArgs& a, float* grads, int T, int W,
 }
 
 cudaError_t launch_setup(const float* params, int BT, int W, int H, float sigma,
-                         int tape_semantics, TriRec* recs, cudaStream_t s) {
+                         int tape_semantics, TriRec* recs, cudaStream_t s, int4* boxes) {
   if (BT == 0) return cudaSuccess;
   const int blocks = (BT + kSetupThreads - 1) / kSetupThreads;
-  dr_setup_kernel<<<blocks, kSetupThreads, 0, s>>>(params, BT, W, H, sigma, tape_semantics, recs);
+  dr_setup_kernel<<<blocks, kSetupThreads, 0, s>>>(params, BT, W, H, sigma, tape_semantics, recs,
+                                                   boxes);
   return cudaGetLastError();
 }
 

@@ -422,9 +422,9 @@ DR_API dr_status dr_loss_backward_timed(dr_ctx* ctx, const float* params,
 DR_API uint64_t dr_tape_bytes(uint64_t n_tris, uint64_t width, uint64_t height);
 
 /* Device scratch a context holds for a loss or gradient call of B scenes of T
- * triangles at H x W (triangle records, loss partials and counters, and the
- * triangle-split state when the call is too small to fill the GPU). No
- * reference counterpart. Returns 0 for invalid sizes. */
+ * triangles at H x W (triangle records and their packed boxes, loss partials
+ * and counters, and the triangle-split state when the call is too small to
+ * fill the GPU). No reference counterpart. Returns 0 for invalid sizes. */
 DR_API uint64_t dr_scratch_bytes(dr_ctx* ctx, int B, int T, int H, int W);
 
 /* GpuRasterizer::is_discrete (diffrast-gpu/src/lib.rs:379-388): 1 for a

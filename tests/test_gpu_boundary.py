@@ -95,8 +95,9 @@ def test_device_queries_and_sizes(native):
     small = native.scratch_bytes(1, 64, 64, 64)   # one small scene: triangle split state
     large = native.scratch_bytes(32, 128, 256, 256)
     assert small > 0 and large > 0
-    # 160-byte records, 8-byte loss partials per tile and 4-byte counters per scene.
-    assert large == 32 * 128 * 160 + 32 * 256 * 8 + 32 * 4
+    # 160-byte records and their 16-byte packed boxes, 8-byte loss partials per tile
+    # and 4-byte counters per scene.
+    assert large == 32 * 128 * (160 + 16) + 32 * 256 * 8 + 32 * 4
 
 
 def test_device_memory_helpers_round_trip(native):
