@@ -151,7 +151,7 @@ def test_config3_torch_op_full_batch(native, oracle):
     t_hwc = targets.permute(0, 2, 3, 1).contiguous().cpu().numpy()
     ref_l, ref_g, ref_img = oracle.backward_batch(p_np, t_hwc, 0.0015, want_images=True)
     assert_images_close(host(img).transpose(0, 2, 3, 1), ref_img, "config 3 render")
-    np.testing.assert_allclose(float(loss), float(np.mean(ref_l)), rtol=1e-5)
+    np.testing.assert_allclose(float(loss.detach()), float(np.mean(ref_l)), rtol=1e-5)
     # F.mse_loss averages over the whole batch: the per-scene gradients / B.
     assert_grads_close(host(q.grad), ref_g / 256, "config 3 grads")
     report("config3", image_max_abs=float(np.nanmax(np.abs(host(img).transpose(0, 2, 3, 1) -
