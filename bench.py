@@ -132,17 +132,45 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines = []
+        self.first = 0
+        self.window = "timed region"
 
     def start(self):
+        """Starts sampling every 50 ms and returns once the first sample is in
+        (at most 5 s), so that nvidia-smi's own start-up stays outside the
+        timed region; samples before the next mark() are not counted."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def mark(self):
+        """The timed region starts: count samples from here on."""
+        self.first = len(self.lines)
+
+    def samples(self) -> int:
+        return len(self.lines) - self.first
+
+    def extend(self, step, want: int = 2, limit_s: float = 2.0):
+        """A timed region shorter than the sampling interval may hold no sample:
+        keep running the same step, untimed, until `want` samples arrive (at
+        most limit_s), and say so in the line."""
+        if self.proc is None or self.samples() >= want:
+            return
+        self.window = "timed steps, continued untimed until two samples arrived"
+        t0 = time.time()
+        while (self.samples() < want and time.time() - t0 < limit_s
+               and self.proc.poll() is None):
+            step()
 
     def _read(self):
         for line in self.proc.stdout:
@@ -157,7 +185,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         rows = []
-        for ln in self.lines:
+        for ln in self.lines[self.first:]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -171,7 +199,7 @@ class ClockSampler:
         reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r)
                           if v.lower() == "active"})
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "window": self.window}
 
 
 def peaks():
@@ -633,10 +661,11 @@ def main():
     torch.cuda.synchronize(dev)
 
     clocks = ClockSampler(local)
+    clocks.start()
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    clocks.start()
+    clocks.mark()
     times = []
     for _ in range(args.steps):
         flush.fill_(1)
@@ -650,6 +679,13 @@ def main():
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
+
+    def untimed():
+        flush.fill_(1)
+        step()
+        torch.cuda.synchronize(dev)
+
+    clocks.extend(untimed)
     clock_info = clocks.stop()
     total_ms = sum(a.elapsed_time(b) for a, b in times)
     t_ms = torch.tensor([total_ms], dtype=torch.float64, device=dev)
