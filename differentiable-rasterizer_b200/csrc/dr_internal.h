@@ -66,6 +66,9 @@ struct RasterArgs {
   long long fit_patience;     // < 0: none
   float fit_min_delta;
   int fit_iter;
+  // Tile kernel launch order: nonzero -> tiles in rings around the canvas
+  // centre, else central rows first (set per launch by the tile launcher).
+  int tile_rings;
 };
 
 struct AdamArgs {
