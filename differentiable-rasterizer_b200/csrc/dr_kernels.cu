@@ -1999,11 +1999,15 @@ static int device_sms() {
 }
 
 // The region kernel when the whole list fits one chunk (T <= kChunk) and the
-// launch fills at least one wave of its CTAs (4 per SM): a region CTA works
-// two tiles, so with fewer CTAs the slowest one sets the time and the tile
-// kernel's finer grid is faster (measured at 256^2, T = 128: 4 scenes, 512
-// region CTAs, take 0.133 ms on the tile kernel and 0.152 ms on the region
-// kernel; 8 scenes, 1024 CTAs, 0.199 and 0.189 ms). Otherwise the tile kernel.
+// launch fills at least two waves of its CTAs (4 per SM): a region CTA works
+// two tiles, so with fewer CTAs the slowest ones set the time and the tile
+// kernel's finer grid, launched in rings, is faster. Measured at 256^2,
+// T = 128 (loss + backward): 6 scenes (768 region CTAs) 0.142 ms on the tile
+// kernel against 0.171 on the region kernel, 8 scenes (1024) 0.177 against
+// 0.187, 11 scenes (1408) 0.232 on both, 12 scenes (1536) 0.251 against 0.247,
+// 16 scenes 0.321 against 0.306; at 128^2 with 32 scenes (1024 region CTAs)
+// 0.223 against 0.237 (T = 128) and 0.097 against 0.095 (T = 32). Otherwise
+// the tile kernel.
 // Regions of 2 x 1 tiles: a 2 x 2 region CTA averaged ~150 us at the headline
 // size (3.5 waves), and SMs that ran out of CTAs idled for up to 100 us while
 // the last ones finished. Halving the unit halves that tail; the list is
@@ -2014,7 +2018,7 @@ static long long region_ctas(int B, int tiles_x, int tile_rows) {
          ((tile_rows + kRegionRows - 1) / kRegionRows) * B;
 }
 static bool use_region_kernel(int B, int T, int tiles_x, int tile_rows) {
-  return T <= kChunk && region_ctas(B, tiles_x, tile_rows) >= 4LL * device_sms();
+  return T <= kChunk && region_ctas(B, tiles_x, tile_rows) >= 8LL * device_sms();
 }
 int raster_path(int B, int T, int tiles_x, int tile_rows, int split_k) {
   if (split_k > 1) return 2;

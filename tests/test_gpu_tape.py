@@ -111,10 +111,11 @@ def test_rasterize_backward_uses_the_tape(native, oracle):
     from conftest import assert_grads_close
 
     p = headline_like(B=32, T=64)
-    target = torch.rand((32, 3, 128, 128), device="cuda",
+    assert native.query_path(32, 64, 256, 256) == native.PATH_REGION  # the tape is kept
+    target = torch.rand((32, 3, 256, 256), device="cuda",
                         generator=torch.Generator(device="cuda").manual_seed(5))
     q = p.clone().requires_grad_(True)
-    loss = torch.nn.functional.mse_loss(torch_layer.rasterize(q, 128, 128, 0.0015), target)
+    loss = torch.nn.functional.mse_loss(torch_layer.rasterize(q, 256, 256, 0.0015), target)
     loss.backward()
     tgt_hwc = target.permute(0, 2, 3, 1).contiguous().cpu().numpy()
     ref_l, ref_g = oracle.backward_batch(p.cpu().numpy(), tgt_hwc, 0.0015)
